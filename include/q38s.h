@@ -1,0 +1,306 @@
+/*
+ * q38s -- C ABI of the B200 token-sampling engine.
+ *
+ * This is the drop-in boundary for the reference runtime's sampler
+ * (src/sampling.cc + include/q38/sampling.h of the reference).  Every entry
+ * point takes plain pointers and sizes, returns a status code and never lets
+ * a C++ exception cross the ABI.  Status codes map one to one onto the
+ * exception classes the reference throws (sampling.cc:43-71, 105-117,
+ * 148-166); q38s_last_error() returns the reference's message text for the
+ * calling thread's last failure.
+ *
+ * Two families of calls:
+ *   q38s_sampler_*  one session, host or device logits: the exact semantics
+ *                   of q38::TransactionalSampler (sampling.h:52-75).  The C++
+ *                   class in include/q38/sampling.h is a thin wrapper over it.
+ *   q38s_batch_*    many sessions ("rows") resident on one GPU, device
+ *                   logits, per-row parameters (SamplingConfigV2 adds min_p),
+ *                   per-row status words, no host synchronisation.
+ * plus speculative (MTP) verification, vocab-sharded sampling and greedy
+ * argmax.
+ *
+ * Threading: like the reference (executor.cc:455, :538) a sampler or batch
+ * is not thread-safe; one host thread drives it.  Calls on a batch are
+ * ordered on the CUDA stream passed in (NULL = the legacy default stream).
+ */
+#ifndef Q38S_H
+#define Q38S_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (return value of every entry point) ------------------ */
+#define Q38S_OK 0
+#define Q38S_INVALID_ARGUMENT 1 /* std::invalid_argument in the reference */
+#define Q38S_LOGIC_ERROR 2      /* std::logic_error                       */
+#define Q38S_RUNTIME_ERROR 3    /* std::runtime_error                     */
+#define Q38S_CUDA_ERROR 4       /* CUDA runtime failure                   */
+#define Q38S_OUT_OF_MEMORY 5
+#define Q38S_TIMEOUT 6          /* a bounded device wait ran out          */
+
+/* ---- per-row status words written by the kernels ----------------------- */
+#define Q38S_ROW_OK 0
+#define Q38S_ROW_NO_FINITE 1     /* "sampler has no finite candidate logits"  (sampling.cc:105-106) */
+#define Q38S_ROW_NORMALIZATION 2 /* "sampler probability normalization failed" (sampling.cc:116-117) */
+#define Q38S_ROW_STATE_MISMATCH 3 /* "sampler decision does not match committed state" (sampling.cc:149-153) */
+#define Q38S_ROW_TIMEOUT 4       /* bounded wait for a TMA copy ran out */
+#define Q38S_ROW_BAD_TOKEN 5     /* committed token outside the vocabulary (sampling.cc:164-165) */
+
+/* ---- logits element types: q38::DType (contracts.h:19-26) -------------- */
+#define Q38S_DTYPE_BF16 1
+#define Q38S_DTYPE_F32 2
+
+/* ---- modes: q38::SamplingModeV1 (sampling.h:14-17) ---------------------- */
+#define Q38S_MODE_GREEDY 0
+#define Q38S_MODE_TOP_K_TOP_P 1
+
+/* SamplingConfigV1 (sampling.h:19-29), 40 bytes, identical layout. */
+typedef struct q38s_sampling_config_v1 {
+    uint16_t mode;
+    uint16_t version; /* must be 1 */
+    uint32_t top_k;   /* 0 = off */
+    float top_p;
+    float temperature;
+    float repetition_penalty;
+    float frequency_penalty;
+    float presence_penalty;
+    uint32_t reserved_; /* padding of the reference struct */
+    uint64_t seed;
+} q38s_sampling_config_v1;
+
+/* SamplingConfigV2: V1 plus min_p in V1's padding word; version must be 2.
+ * min_p in [0, 1]; 0 disables it and reduces exactly to V1. */
+typedef struct q38s_sampling_config_v2 {
+    uint16_t mode;
+    uint16_t version; /* must be 2 */
+    uint32_t top_k;
+    float top_p;
+    float temperature;
+    float repetition_penalty;
+    float frequency_penalty;
+    float presence_penalty;
+    float min_p;
+    uint64_t seed;
+} q38s_sampling_config_v2;
+
+/* SamplerStateV1 (sampling.h:31-39), 40 bytes, identical layout. */
+typedef struct q38s_sampler_state_v1 {
+    uint32_t magic; /* fourcc('Q','3','8','S') */
+    uint16_t version;
+    uint16_t header_bytes;
+    uint64_t rng_state;
+    uint64_t sampled_tokens;
+    uint64_t canonical_tokens;
+    uint64_t penalty_checksum;
+} q38s_sampler_state_v1;
+
+/* SamplerDecisionV1 (sampling.h:41-45), 24 bytes, identical layout; the
+ * reference's padding word carries the row status (Q38S_ROW_*). */
+typedef struct q38s_decision_v1 {
+    int32_t token;
+    int32_t status;
+    uint64_t rng_before;
+    uint64_t rng_after;
+} q38s_decision_v1;
+
+/* One (value, token) pair of a top-k candidate list. */
+typedef struct q38s_candidate {
+    float value; /* logit after penalties and temperature */
+    int32_t token;
+} q38s_candidate;
+
+/* Optional per-row distribution output of q38s_batch_prepare (device
+ * arrays, `rows * capacity` entries each; any pointer may be NULL).
+ * Row r receives its sorted candidates after top-k and min-p (tokens,
+ * values), the probabilities w_i / total over the retained top-p prefix,
+ * the candidate and retained counts and the totals of sampling.cc:110-134. */
+typedef struct q38s_distribution {
+    uint32_t capacity;
+    int32_t* tokens;
+    float* values;
+    double* probs;
+    uint32_t* n_candidates;
+    uint32_t* n_retained;
+    double* total;
+    double* draw;
+} q38s_distribution;
+
+/* Additional penalty tokens of one prepare call (sampling.cc:67-73), per
+ * row, on the device: row r uses tokens[offsets[r] .. offsets[r+1]).
+ * Duplicates count once per occurrence, as in the reference. */
+typedef struct q38s_penalty_extra {
+    const int32_t* tokens;
+    const uint32_t* offsets; /* rows + 1 entries */
+} q38s_penalty_extra;
+
+typedef struct q38s_sampler q38s_sampler;
+typedef struct q38s_batch q38s_batch;
+
+/* ------------------------------------------------------------------------
+ * Library
+ * ---------------------------------------------------------------------- */
+/* Message of the calling thread's last failing call ("" if none). */
+const char* q38s_last_error(void);
+/* Build identification ("q38s <version> sm_100a"). */
+const char* q38s_version(void);
+
+/* ------------------------------------------------------------------------
+ * Single session: q38::TransactionalSampler (sampling.h:52-75)
+ * ---------------------------------------------------------------------- */
+/* Replaces TransactionalSampler::TransactionalSampler (sampling.cc:40-57).
+ * Validates exactly as the reference (Q38S_INVALID_ARGUMENT with its
+ * messages), allocates the device penalty state on `device`. */
+int q38s_sampler_create(int device, uint32_t vocabulary,
+                        const q38s_sampling_config_v1* config,
+                        q38s_sampler** out);
+/* Same with a V2 config (min_p). */
+int q38s_sampler_create_v2(int device, uint32_t vocabulary,
+                           const q38s_sampling_config_v2* config,
+                           q38s_sampler** out);
+void q38s_sampler_destroy(q38s_sampler* sampler);
+
+/* Replaces TransactionalSampler::prepare (sampling.cc:59-146) for HOST bf16
+ * logits (StageOutput::logits_bf16, backend.h:143): copies them to the GPU,
+ * samples, returns the decision.  const: no state changes. */
+int q38s_sampler_prepare(const q38s_sampler* sampler,
+                         const uint16_t* logits_bf16, size_t count,
+                         const int32_t* additional_penalty_tokens,
+                         size_t n_additional, q38s_decision_v1* out);
+/* prepare() on logits already on the device (the producer's
+ * workspace.logits, cuda_backend.cu:957), bf16 or fp32.  Only the decision
+ * (24 bytes) crosses PCIe. */
+int q38s_sampler_prepare_device(const q38s_sampler* sampler,
+                                const void* logits, uint16_t dtype,
+                                size_t count,
+                                const int32_t* additional_penalty_tokens,
+                                size_t n_additional, q38s_decision_v1* out,
+                                void* stream);
+/* Replaces TransactionalSampler::commit (sampling.cc:148-156). */
+int q38s_sampler_commit(q38s_sampler* sampler, const q38s_decision_v1* d);
+/* Replaces commit_tokens / commit_token (sampling.cc:158-172). */
+int q38s_sampler_commit_tokens(q38s_sampler* sampler, const int32_t* tokens,
+                               size_t count);
+/* Replaces reset (sampling.cc:174-178). */
+int q38s_sampler_reset(q38s_sampler* sampler);
+/* state() / config() accessors (sampling.h:60-61). */
+int q38s_sampler_state(const q38s_sampler* sampler,
+                       q38s_sampler_state_v1* out);
+int q38s_sampler_config(const q38s_sampler* sampler,
+                        q38s_sampling_config_v1* out);
+
+/* ------------------------------------------------------------------------
+ * Batch: one TransactionalSampler per row, all rows on one GPU.
+ * ---------------------------------------------------------------------- */
+/* `rows` samplers over `vocabulary` tokens (sampling.cc:40-57 per row). */
+int q38s_batch_create(int device, uint32_t vocabulary, uint32_t rows,
+                      const q38s_sampling_config_v2* configs,
+                      q38s_batch** out);
+/* A batch that owns the contiguous vocabulary columns [col_begin,
+ * col_begin + columns) of a `vocabulary`-wide LM head (vocab-parallel
+ * sampling).  Penalty state covers only the owned columns. */
+int q38s_batch_create_shard(int device, uint32_t vocabulary,
+                            uint32_t col_begin, uint32_t columns,
+                            uint32_t rows,
+                            const q38s_sampling_config_v2* configs,
+                            q38s_batch** out);
+void q38s_batch_destroy(q38s_batch* batch);
+uint32_t q38s_batch_rows(const q38s_batch* batch);
+
+/* reset() of every row (sampling.cc:174-178). */
+int q38s_batch_reset(q38s_batch* batch, void* stream);
+/* Copies the rows' SamplerStateV1 to host memory (synchronises stream). */
+int q38s_batch_states(const q38s_batch* batch, q38s_sampler_state_v1* out,
+                      void* stream);
+/* commit_tokens() per row (sampling.cc:158-172): row r appends device
+ * tokens[offsets[r] .. offsets[r+1]).  Tokens outside the vocabulary (or the
+ * shard's columns, for a shard batch) set that row's status to
+ * Q38S_ROW_BAD_TOKEN in `status` (may be NULL) and are skipped. */
+int q38s_batch_commit_tokens(q38s_batch* batch, const int32_t* tokens,
+                             const uint32_t* offsets, int32_t* status,
+                             void* stream);
+/* prepare() for every row (sampling.cc:59-146) over device logits (row r at
+ * logits + r * row_stride elements).  Writes decisions[r] (token, status,
+ * rng pair); mutates nothing.  `extra` and `dist` may be NULL. */
+int q38s_batch_prepare(const q38s_batch* batch, const void* logits,
+                       uint16_t dtype, uint64_t row_stride,
+                       const q38s_penalty_extra* extra,
+                       q38s_decision_v1* decisions,
+                       const q38s_distribution* dist, void* stream);
+/* commit() for every row (sampling.cc:148-156).  A decision that does not
+ * match the row's state sets decisions[r].status = Q38S_ROW_STATE_MISMATCH
+ * and leaves the row unchanged. */
+int q38s_batch_commit(q38s_batch* batch, q38s_decision_v1* decisions,
+                      void* stream);
+/* One decode step for every row: prepare, then commit the decision and the
+ * sampled token (the sequence of DualStageExecutor::decode_one,
+ * executor.cc:672-687, sampler calls at :455-459, :538, :684) in one launch. */
+int q38s_batch_sample_commit(q38s_batch* batch, const void* logits,
+                             uint16_t dtype, uint64_t row_stride,
+                             q38s_decision_v1* decisions, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Speculative (MTP) verification -- the entry DualStageExecutor::
+ * speculative_step would call instead of its sampled-mode fallback
+ * (executor.cc:696-699); draft width <= 64 (backend.h:17).
+ * ---------------------------------------------------------------------- */
+typedef struct q38s_mtp_result {
+    int32_t tokens[65];   /* accepted drafts, then one sampled token */
+    uint32_t n_tokens;    /* n_accepted + 1 */
+    uint32_t n_accepted;
+    int32_t status;       /* Q38S_ROW_* */
+    uint64_t rng_before;
+    uint64_t rng_after;   /* rng_before + n_tokens * 0x9e3779b97f4a7c15 */
+} q38s_mtp_result;
+
+/* Verifies n_draft draft tokens of batch row `row` against n_draft + 1
+ * target rows (target + i * row_stride) and n_draft draft rows.  Target
+ * and draft row i are transformed with the row's parameters and penalty
+ * state plus draft_tokens[0..i) as additional penalty tokens.  Draft i is
+ * accepted iff u_i * q_i(d_i) < p_i(d_i) with u_i = uniform01(s_i ^
+ * 0xd6e8feb86659fd93), s_i = rng_state + (i + 1) * gamma; on the first
+ * rejection the token is drawn from max(0, p_i - q_i) with uniform01(s_i);
+ * if all are accepted the bonus token is the reference draw from
+ * p_n_draft.  Writes *result on the device; mutates nothing (commit with
+ * q38s_batch_commit_tokens and the returned rng_after). */
+int q38s_mtp_verify(const q38s_batch* batch, uint32_t row,
+                    const void* target, const void* draft, uint16_t dtype,
+                    uint64_t row_stride, const int32_t* draft_tokens,
+                    uint32_t n_draft, q38s_mtp_result* result,
+                    void* stream);
+
+/* ------------------------------------------------------------------------
+ * Vocab-parallel sampling (no reference counterpart; the reference runs its
+ * LM head whole on one GPU, cuda_backend.cu:1665-1669).
+ * ---------------------------------------------------------------------- */
+/* Local top-`k_local` candidates of every row over this shard's columns,
+ * after the row's penalties and temperature, canonical order (value desc,
+ * token asc), global token ids: out[r * k_local + j]. */
+int q38s_shard_topk(const q38s_batch* shard, const void* logits,
+                    uint16_t dtype, uint64_t row_stride, uint32_t k_local,
+                    q38s_candidate* out, void* stream);
+/* Merges n_shards gathered candidate lists (gathered[(s * rows + r) *
+ * k_local + j], shards in column order) into each row's global top-k, then
+ * min-p, top-p and the seeded draw with the row's parameters (rows must
+ * have 0 < top_k <= k_local).  Writes decisions[r]; mutates nothing. */
+int q38s_shard_merge_sample(const q38s_batch* shard,
+                            const q38s_candidate* gathered,
+                            uint32_t n_shards, uint32_t k_local,
+                            q38s_decision_v1* decisions, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Greedy: replaces cuda_argmax_bf16 (cuda/q38_kernels.cu:656-665,
+ * kernel :320-356): index of the largest bf16 value, lowest index on ties,
+ * NaN never selected.
+ * ---------------------------------------------------------------------- */
+int q38s_argmax_bf16(const uint16_t* logits, uint32_t count, int32_t* output,
+                     void* stream, int device);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* Q38S_H */

@@ -1,0 +1,102 @@
+// Kernel-side data structures shared by q38s_sample.cu and the host ABI.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "q38s.h"
+#include "q38s_device.cuh"
+
+namespace q38s {
+
+constexpr int kThreads = 256;        // threads per CTA
+constexpr int kMaxCluster = 8;       // CTAs per row (portable cluster size)
+constexpr int kCap = 1024;           // per-CTA candidate buffer (rank keys)
+constexpr int kLeaderCap = 1024;     // merged candidates held by the leader
+constexpr int kFastTopK = 128;       // largest top_k served by the fast path
+constexpr int kPieces = 4;           // TMA pieces per chunk
+constexpr int kHistBins = 256;       // radix digit histogram (general path)
+constexpr uint32_t kMaxGeneralVocab = 1u << 20;  // fixed-point mass headroom
+
+// Per-row mutable sampler state: SamplerStateV1 (sampling.h:31-39) minus
+// its constant header words.
+struct RowState {
+    uint64_t rng_state;
+    uint64_t sampled_tokens;
+    uint64_t canonical_tokens;
+    uint64_t penalty_checksum;
+};
+
+enum Mode : int {
+    kModePrepare = 0,       // decisions only
+    kModeSampleCommit = 1,  // decisions + commit + commit_token
+    kModeShardTopK = 2,     // emit the local top-k candidate list
+    kModeDistribution = 3,  // decisions + per-row distribution (+ MTP)
+};
+
+// Arguments of the row-sampling kernel.  A "virtual row" is one unit of
+// work: normally one batch row; for speculative verification one target or
+// draft row of a single session.
+struct SampleArgs {
+    // virtual row v < split reads logits + v * row_stride elements,
+    // v >= split reads logits2 + (v - split) * row_stride.
+    const void* logits;
+    const void* logits2;
+    uint32_t split;
+    uint64_t row_stride;
+    int dtype;            // Q38S_DTYPE_*
+    int use_tma;          // rows are 16-byte aligned
+    uint32_t vocab;       // columns of this batch (shard width or full vocab)
+    uint32_t full_vocab;  // vocabulary of the whole LM head
+    uint32_t col_begin;   // global token id of column 0
+    uint32_t vrows;
+    int mode;
+    // per state row
+    const RowParams* params;
+    RowState* state;
+    uint32_t* bitmap;     // state row r: bitmap + r * bitmap_words
+    uint32_t bitmap_words;
+    uint32_t* counts;     // state row r: counts + r * vocab (or null)
+    // virtual row -> state row: vrow_state_const if != ~0u, else identity
+    uint32_t vrow_state_const;
+    // the draw of virtual row v uses rng_state + (1 + rng_offset(v)) * gamma,
+    // rng_offset(v) = rng_step ? (v < split ? v : v - split) : 0
+    int rng_step;
+    // additional penalty tokens: 0 none; 1 CSR (extra_offsets); 2 prefix of
+    // extra_tokens of length (v < split ? v : v - split)
+    int extra_mode;
+    const int32_t* extra_tokens;
+    const uint32_t* extra_offsets;
+    // outputs
+    q38s_decision_v1* decisions;
+    q38s_distribution dist;
+    q38s_candidate* topk_out;  // kModeShardTopK: vrows * k_out entries
+    uint32_t k_out;
+    // general-path scratch: one vocab-sized key array per virtual row
+    uint32_t* scratch;
+    // speculative verification, run by the last row to finish
+    q38s_mtp_result* mtp;
+    uint32_t n_draft;
+    const int32_t* draft_tokens;
+    uint32_t* ticket;
+};
+
+// Launchers (q38s_sample.cu).  All return a cudaError_t as int.
+int launch_sample(const SampleArgs& a, void* stream);
+int launch_commit_tokens(RowState* state, uint32_t* bitmap, uint32_t bitmap_words,
+                         uint32_t* counts, uint32_t vocab, uint32_t col_begin,
+                         uint32_t rows, const int32_t* tokens, const uint32_t* offsets,
+                         int32_t* status, void* stream);
+int launch_commit(RowState* state, uint32_t rows, uint32_t vocab,
+                  q38s_decision_v1* decisions, void* stream);
+int launch_reset_states(RowState* state, const uint64_t* seeds, uint32_t rows,
+                        void* stream);
+int launch_shard_merge(const RowParams* params, const RowState* state, uint32_t rows,
+                       const q38s_candidate* gathered, uint32_t n_shards,
+                       uint32_t k_local, q38s_decision_v1* decisions, void* stream);
+int launch_argmax_bf16(const uint16_t* logits, uint32_t count, int32_t* out,
+                       void* stream);
+size_t sample_smem_bytes(uint32_t vocab, int dtype, int cluster);
+int sample_cluster_size(uint32_t vocab);
+
+}  // namespace q38s
