@@ -145,6 +145,10 @@ struct q38s_batch {
     uint32_t* d_mtp_ncand = nullptr;
     q38s_decision_v1* d_mtp_dec = nullptr;
     uint32_t* d_ticket = nullptr;
+    // streaming sampler: per-unit segment lists and per-virtual-row tickets
+    uint64_t* d_seg_keys = nullptr;
+    uint32_t* d_seg_hdr = nullptr;
+    uint32_t* d_row_ticket = nullptr;
 };
 
 namespace {
@@ -167,6 +171,9 @@ void free_batch(q38s_batch* b) {
     cudaFree(b->d_mtp_ncand);
     cudaFree(b->d_mtp_dec);
     cudaFree(b->d_ticket);
+    cudaFree(b->d_seg_keys);
+    cudaFree(b->d_seg_hdr);
+    cudaFree(b->d_row_ticket);
     delete b;
 }
 
@@ -218,6 +225,12 @@ int create_batch(int device, uint32_t full_vocab, uint32_t col_begin, uint32_t c
     alloc(reinterpret_cast<void**>(&b->d_scratch),
           sizeof(uint32_t) * static_cast<size_t>(columns) * rows);
     b->scratch_rows = rows;
+    const size_t tickets = std::max<size_t>(rows, kMtpRows);
+    alloc(reinterpret_cast<void**>(&b->d_seg_keys),
+          sizeof(uint64_t) * static_cast<size_t>(kMaxSegUnits) * kSegCap);
+    alloc(reinterpret_cast<void**>(&b->d_seg_hdr), sizeof(uint32_t) * 4 * kMaxSegUnits);
+    alloc(reinterpret_cast<void**>(&b->d_row_ticket), sizeof(uint32_t) * tickets);
+    if (e == cudaSuccess) e = cudaMemset(b->d_row_ticket, 0, sizeof(uint32_t) * tickets);
     if (e == cudaSuccess)
         e = cudaMemcpy(b->d_params, params.data(), sizeof(RowParams) * rows,
                        cudaMemcpyHostToDevice);
@@ -272,11 +285,17 @@ SampleArgs base_args(const q38s_batch* b, const void* logits, uint16_t dtype,
     a.counts = b->d_counts;
     a.vrow_state_const = ~0u;
     a.scratch = b->d_scratch;
+    a.seg_keys = b->d_seg_keys;
+    a.seg_hdr = b->d_seg_hdr;
+    a.row_ticket = b->d_row_ticket;
     return a;
 }
 
-int launch_checked(const SampleArgs& a, void* stream, const char* what) {
-    const int e = launch_sample(a, stream);
+// Every row-sampling call goes through the streaming sampler; the number
+// of column segments per row follows from the number of virtual rows.
+int launch_checked(SampleArgs a, void* stream, const char* what, int device) {
+    a.segs = stream_segments(a.vrows, a.vocab, device);
+    const int e = launch_stream(a, stream);
     if (e != cudaSuccess) return cuda_fail(static_cast<cudaError_t>(e), what);
     return ok();
 }
@@ -370,7 +389,7 @@ int q38s_batch_prepare(const q38s_batch* b, const void* logits, uint16_t dtype,
         a.dist = *dist;
         a.mode = kModeDistribution;
     }
-    return launch_checked(a, stream, "prepare");
+    return launch_checked(a, stream, "prepare", b->device);
 }
 
 int q38s_batch_sample_commit(q38s_batch* b, const void* logits, uint16_t dtype,
@@ -382,7 +401,7 @@ int q38s_batch_sample_commit(q38s_batch* b, const void* logits, uint16_t dtype,
     SampleArgs a = base_args(b, logits, dtype, row_stride);
     a.decisions = decisions;
     a.mode = kModeSampleCommit;
-    return launch_checked(a, stream, "sample_commit");
+    return launch_checked(a, stream, "sample_commit", b->device);
 }
 
 int q38s_batch_commit(q38s_batch* b, q38s_decision_v1* decisions, void* stream) {
@@ -447,7 +466,7 @@ int q38s_mtp_verify(const q38s_batch* bc, uint32_t row, const void* target, cons
     a.draft_tokens = draft_tokens;
     a.ticket = b->d_ticket;
     if (!(reinterpret_cast<uintptr_t>(draft) % 16 == 0)) a.use_tma = 0;
-    return launch_checked(a, stream, "mtp_verify");
+    return launch_checked(a, stream, "mtp_verify", b->device);
 }
 
 int q38s_shard_topk(const q38s_batch* b, const void* logits, uint16_t dtype,
@@ -461,7 +480,7 @@ int q38s_shard_topk(const q38s_batch* b, const void* logits, uint16_t dtype,
     a.mode = kModeShardTopK;
     a.topk_out = out;
     a.k_out = k_local;
-    return launch_checked(a, stream, "shard_topk");
+    return launch_checked(a, stream, "shard_topk", b->device);
 }
 
 int q38s_shard_merge_sample(const q38s_batch* b, const q38s_candidate* gathered,
@@ -635,7 +654,7 @@ int prepare_common(const q38s_sampler* cs, const void* d_logits, uint16_t dtype,
         a.extra_tokens = s->d_tokens;
         a.extra_offsets = s->d_offsets;
     }
-    rc = launch_checked(a, s->stream, "prepare");
+    rc = launch_checked(a, s->stream, "prepare", s->batch->device);
     if (rc) return rc;
     Q38S_CUDA(cudaMemcpyAsync(s->h_decision, s->d_decision, sizeof(q38s_decision_v1),
                               cudaMemcpyDeviceToHost, s->stream),

@@ -79,9 +79,24 @@ struct SampleArgs {
     uint32_t n_draft;
     const int32_t* draft_tokens;
     uint32_t* ticket;
+    // streaming sampler (q38s_stream.cu): each virtual row is split into
+    // `segs` column segments; a row with segs > 1 parks each segment's
+    // sorted candidate list in seg_keys/seg_hdr (one slot per unit
+    // v * segs + s) and the last segment to finish (row_ticket[v]) merges
+    // them.  row_ticket words are zero between launches.
+    uint32_t segs;
+    uint64_t* seg_keys;   // units * kSegCap rank keys
+    uint32_t* seg_hdr;    // units * 4 words: length, flags, max key, unused
+    uint32_t* row_ticket; // vrows words
 };
 
+// Streaming-sampler limits (q38s_stream.cu).
+constexpr uint32_t kSegCap = 512;       // candidates a segment hands to the merge
+constexpr uint32_t kMaxSegUnits = 512;  // vrows * segs when segs > 1
+
 // Launchers (q38s_sample.cu).  All return a cudaError_t as int.
+int launch_stream(const SampleArgs& a, void* stream);   // streaming sampler
+uint32_t stream_segments(uint32_t vrows, uint32_t vocab, int device);
 int launch_sample(const SampleArgs& a, void* stream);
 int launch_commit_tokens(RowState* state, uint32_t* bitmap, uint32_t bitmap_words,
                          uint32_t* counts, uint32_t vocab, uint32_t col_begin,

@@ -1,0 +1,1717 @@
+// Streaming row sampler for sm_100a: the hot path of every prepare /
+// sample-commit / speculative-verification / vocab-shard call.
+//
+// Work decomposition.  Each virtual row (a batch row, or one target / draft
+// row of a speculative verification) is split into `segs` column segments
+// (whole 128-column blocks).  A unit is one (row, segment) pair; a persistent
+// grid of at most two CTAs per SM walks the units (CTA b takes units b,
+// b + G, b + 2G, ...).  Large batches use one segment per row, so every row
+// is streamed start to finish by one CTA; small batches split rows so the
+// whole GPU pulls HBM.  The last segment of a row to finish (a ticket per
+// row, reset by that CTA) merges the segments' candidate lists.  No CTA ever
+// waits for another.
+//
+// Inside a CTA.  Warp 8 is a producer: one lane streams the CTA's tiles
+// (16 KB of logits each, plus the matching 1 KB slice of the row's penalty
+// bitmap when the row has penalties) through a ring of four shared-memory
+// slots with 1-D TMA bulk copies (no multicast), completion on a `full`
+// mbarrier per slot.  Warps 0-7 consume: they release a slot on its `empty`
+// mbarrier as soon as they have read it, so copies for the next tiles (and
+// the next unit) stay in flight while the consumers do per-row serial work.
+//
+// Per unit the consumers
+//   seed    take each thread's largest raw logit of the first tile, evaluate
+//           it exactly, and derive theta: the k-th largest of those 256
+//           values (a lower bound of the row's k-th largest value) and, for
+//           min-p rows, M + ln(min_p) - slack (M = the largest exact value
+//           seen, a lower bound of the row maximum);
+//   filter  one packed bf16x2 (or f32) maximum over the thread's 32 (16)
+//           logits of a tile is compared with theta's raw-logit bound; only
+//           hits get the reference's exact penalty / temperature arithmetic
+//           (sampling.cc:76-92) and enter a shared-memory buffer as 64-bit
+//           rank keys (value desc, token asc).  theta rises with the running
+//           maximum (min-p) and by exact compaction of the buffer;
+//   finish  exact top-k and min-p cuts of the buffer, a sort, then the
+//           reference's softmax / top-p / draw (sampling.cc:105-145) in
+//           double precision with its sequential summation order.
+// Rows whose candidate sets do not fit (top_k = 0 without min-p, top_k > 256
+// without min-p, mass ties) take the CTA's general path: exact keys of every
+// column in global scratch, radix selection of the top-k / min-p cut, and
+// either an exact gather (kept sets up to 1,024) or a fixed-point
+// mass-weighted selection of the top-p cut and the draw.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "q38s_kernels.cuh"
+
+namespace q38s {
+namespace {
+
+constexpr uint32_t kTileBytes = 16384;           // logits per ring slot
+constexpr uint32_t kTileBm = 1024;               // bitmap bytes per slot (8,192 columns)
+constexpr uint32_t kSlot = kTileBytes + kTileBm;
+constexpr uint32_t kRing = 4;                    // ring slots per CTA
+constexpr int kCons = 256;                       // consumer threads (warps 0-7)
+constexpr int kBlock = kCons + 32;               // + the producer warp
+constexpr uint32_t kBuf = 2048;                  // candidate buffer (rank keys)
+constexpr uint32_t kSlice = kBuf / (kCons / 32);  // candidate slice of one consumer warp
+constexpr uint32_t kShrinkAt = kSlice - 32;      // warp compaction trigger
+constexpr int kWarpPer = kSlice / 32;            // slice entries per lane
+constexpr uint32_t kFinal = kSegCap;             // candidates entering the epilogue
+constexpr uint32_t kGather = 1024;               // exact gather of the general path
+constexpr uint32_t kArea = 32768;                // candidate / epilogue work area
+constexpr double kFix = 8796093022208.0;         // 2^43: fixed-point weight unit
+
+constexpr uint32_t kFOverflow = 1u;
+constexpr uint32_t kFInf = 2u;
+constexpr uint32_t kFTimeout = 4u;
+
+static_assert(kBuf * 8 + kFinal * 8 + 3 * kFinal * 8 <= kArea, "fast-path area");
+
+// Optional per-unit trace (build with -DQ38S_TRACE; off in the product
+// build): 16 words per unit -- global-timer stamps of the unit's phases, its
+// threshold, candidate count, flags and the path that finished it.  The
+// buffer is installed with q38s_trace_install().
+#ifdef Q38S_TRACE
+__device__ unsigned long long* g_trace = nullptr;
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+#define Q38S_TR(u, slot, val)                                                     \
+    do {                                                                          \
+        if (g_trace && threadIdx.x == 0 && (u) < 8192)                            \
+            g_trace[static_cast<size_t>(u) * 16 + (slot)] =                       \
+                static_cast<unsigned long long>(val);                             \
+    } while (0)
+#define Q38S_TT(u, slot) Q38S_TR(u, slot, gtime())
+#else
+#define Q38S_TR(u, slot, val) do { } while (0)
+#define Q38S_TT(u, slot) do { } while (0)
+#endif
+static_assert(kGather * 32 <= kArea, "general-path area");
+
+struct __align__(16) Ctl {
+    uint64_t full[kRing];
+    uint64_t empty[kRing];
+    uint32_t abort_flag;   // set by whichever side gave up waiting
+    uint32_t prod_done;    // producer left its loop
+    uint32_t issued;       // tiles issued by the producer
+    uint32_t n_cand;
+    uint32_t flags;
+    uint32_t mrun;         // running maximum of exact candidate keys
+    uint32_t fail_g;       // first tile a consumer warp gave up waiting for
+    uint32_t wcnt[kCons / 32];  // per-warp slice lengths at the end of a unit
+    uint32_t bc_u32[4];
+    uint64_t bc_u64[2];
+    uint32_t red_u32[kCons / 32];
+    uint64_t red_u64[kCons / 32];
+    uint32_t hist[256];
+    uint64_t hmass[256];
+    uint32_t tkey[kCons];
+    int32_t e_token;
+    int32_t e_status;
+    uint32_t e_n;
+    uint32_t e_r;
+    double e_total;
+    double e_draw;
+};
+
+// ------------------------------------------------------ consumer barriers
+// Named barrier 1 spans exactly the 256 consumer threads; the producer warp
+// never takes part.
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ bool cbar_or(bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred q, s;\n setp.ne.u32 q, %1, 0;\n"
+        " bar.red.or.pred s, 1, 256, q;\n selp.u32 %0, 1, 0, s;\n}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(p))
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Block reductions over the consumers.  The leading barrier keeps a
+// reduction from overwriting red_* while the previous one is still read.
+__device__ uint32_t cmax_u32(uint32_t v, Ctl& c) {
+    v = warp_max_u32(v);
+    cbar();
+    if ((threadIdx.x & 31) == 0) c.red_u32[threadIdx.x >> 5] = v;
+    cbar();
+    uint32_t r = c.red_u32[0];
+    for (int i = 1; i < kCons / 32; ++i) r = max(r, c.red_u32[i]);
+    return r;
+}
+__device__ uint32_t cmin_u32(uint32_t v, Ctl& c) {
+    v = warp_min_u32(v);
+    cbar();
+    if ((threadIdx.x & 31) == 0) c.red_u32[threadIdx.x >> 5] = v;
+    cbar();
+    uint32_t r = c.red_u32[0];
+    for (int i = 1; i < kCons / 32; ++i) r = min(r, c.red_u32[i]);
+    return r;
+}
+__device__ uint32_t cor_u32(uint32_t v, Ctl& c) {
+    for (int o = 16; o > 0; o >>= 1) v |= __shfl_xor_sync(0xffffffffu, v, o);
+    cbar();
+    if ((threadIdx.x & 31) == 0) c.red_u32[threadIdx.x >> 5] = v;
+    cbar();
+    uint32_t r = 0;
+    for (int i = 0; i < kCons / 32; ++i) r |= c.red_u32[i];
+    return r;
+}
+__device__ uint32_t csum_u32(uint32_t v, Ctl& c) {
+    v = warp_sum_u32(v);
+    cbar();
+    if ((threadIdx.x & 31) == 0) c.red_u32[threadIdx.x >> 5] = v;
+    cbar();
+    uint32_t r = 0;
+    for (int i = 0; i < kCons / 32; ++i) r += c.red_u32[i];
+    return r;
+}
+__device__ uint64_t csum_u64(uint64_t v, Ctl& c) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    cbar();
+    if ((threadIdx.x & 31) == 0) c.red_u64[threadIdx.x >> 5] = v;
+    cbar();
+    uint64_t r = 0;
+    for (int i = 0; i < kCons / 32; ++i) r += c.red_u64[i];
+    return r;
+}
+// Exclusive prefix sum over the consumers in thread order; *total gets the sum.
+__device__ uint32_t cscan_excl(uint32_t v, uint32_t* total, Ctl& c) {
+    const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    uint32_t inc = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= static_cast<uint32_t>(o)) inc += y;
+    }
+    cbar();
+    if (lane == 31) c.red_u32[w] = inc;
+    cbar();
+    uint32_t before = 0, all = 0;
+    for (uint32_t i = 0; i < kCons / 32; ++i) {
+        const uint32_t x = c.red_u32[i];
+        if (i < w) before += x;
+        all += x;
+    }
+    *total = all;
+    return before + inc - v;
+}
+
+// ------------------------------------------------------------ row context
+struct Row {
+    uint32_t v;           // virtual row
+    uint32_t srow;        // state row
+    RowParams p;
+    uint64_t rng_before;
+    uint32_t k_eff;       // 0: no top-k truncation
+    bool pen, nonmono, freq, minp;
+    const uint32_t* gbm;  // the state row's penalty bitmap
+    const uint32_t* counts_row;
+    const int32_t* extra; // additional penalty tokens (global token ids)
+    uint32_t n_extra;
+    double lnmp;          // log(min_p) for min-p rows
+};
+
+__device__ __forceinline__ uint32_t state_row(const SampleArgs& a, uint32_t v) {
+    return a.vrow_state_const != ~0u ? a.vrow_state_const : v;
+}
+
+__device__ void load_row(const SampleArgs& a, uint32_t v, Row& r) {
+    r.v = v;
+    r.srow = state_row(a, v);
+    r.p = a.params[r.srow];
+    const uint32_t off = v < a.split ? v : v - a.split;
+    r.rng_before = a.state[r.srow].rng_state +
+                   (a.rng_step ? static_cast<uint64_t>(off) * kGamma : 0ull);
+    r.pen = (r.p.flags & kFlagPenalties) != 0;
+    r.nonmono = (r.p.flags & kFlagNonMonotone) != 0;
+    r.freq = (r.p.flags & kFlagFrequency) != 0;
+    r.minp = a.mode != kModeShardTopK && r.p.min_p > 0.0f;
+    r.lnmp = r.minp ? log(static_cast<double>(r.p.min_p)) : 0.0;
+    r.gbm = a.bitmap + static_cast<size_t>(r.srow) * a.bitmap_words;
+    r.counts_row = a.counts ? a.counts + static_cast<size_t>(r.srow) * a.vocab : nullptr;
+    r.extra = nullptr;
+    r.n_extra = 0;
+    if (a.extra_mode == 1) {
+        r.extra = a.extra_tokens + a.extra_offsets[v];
+        r.n_extra = a.extra_offsets[v + 1] - a.extra_offsets[v];
+    } else if (a.extra_mode == 2) {
+        r.extra = a.extra_tokens;
+        r.n_extra = off;
+    }
+    if (a.mode == kModeShardTopK) r.k_eff = a.k_out >= a.vocab ? 0u : a.k_out;
+    else r.k_eff = (r.p.top_k == 0 || r.p.top_k >= a.full_vocab) ? 0u : r.p.top_k;
+}
+
+// Occurrences of global token `tok` among this call's additional tokens.
+__device__ __forceinline__ uint64_t extra_count(const Row& r, uint32_t tok) {
+    uint64_t n = 0;
+    for (uint32_t e = 0; e < r.n_extra; ++e) n += static_cast<uint32_t>(r.extra[e]) == tok;
+    return n;
+}
+
+template <int DT>
+__device__ __forceinline__ const unsigned char* row_ptr(const SampleArgs& a, uint32_t v) {
+    constexpr uint32_t es = DT == Q38S_DTYPE_BF16 ? 2u : 4u;
+    return v < a.split
+        ? static_cast<const unsigned char*>(a.logits) + static_cast<size_t>(v) * a.row_stride * es
+        : static_cast<const unsigned char*>(a.logits2) +
+              static_cast<size_t>(v - a.split) * a.row_stride * es;
+}
+
+template <int DT>
+__device__ __forceinline__ float load_elem(const unsigned char* base, uint32_t j) {
+    if (DT == Q38S_DTYPE_BF16)
+        return __uint_as_float(static_cast<uint32_t>(
+                                   reinterpret_cast<const uint16_t*>(base)[j]) << 16);
+    return reinterpret_cast<const float*>(base)[j];
+}
+
+// Element e of a 16-byte vector (e is a compile-time constant after unrolling).
+template <int DT>
+__device__ __forceinline__ float vec_elem(const uint4& w, int e) {
+    if (DT == Q38S_DTYPE_BF16) {
+        const uint32_t word = e < 2 ? w.x : e < 4 ? w.y : e < 6 ? w.z : w.w;
+        return (e & 1) ? bf16_hi(word) : bf16_lo(word);
+    }
+    return __uint_as_float(e == 0 ? w.x : e == 1 ? w.y : e == 2 ? w.z : w.w);
+}
+
+template <int DT>
+__device__ __forceinline__ float vec_max(const uint4& w) {
+    if (DT == Q38S_DTYPE_BF16) {
+        const __nv_bfloat162 m =
+            __hmax2(__hmax2(*reinterpret_cast<const __nv_bfloat162*>(&w.x),
+                            *reinterpret_cast<const __nv_bfloat162*>(&w.y)),
+                    __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&w.z),
+                            *reinterpret_cast<const __nv_bfloat162*>(&w.w)));
+        return fmaxf(__low2float(m), __high2float(m));
+    }
+    return fmaxf(fmaxf(__uint_as_float(w.x), __uint_as_float(w.y)),
+                 fmaxf(__uint_as_float(w.z), __uint_as_float(w.w)));
+}
+
+// Exact transformed value of a tile element (sampling.cc:76-92): the
+// penalised bit comes from the slot's bitmap copy (which carries this
+// call's additional tokens), the frequency count from global memory.  One
+// out-of-line copy of the IEEE division sequences keeps them out of the
+// unrolled streaming loop, so a warp that takes this (rare) path does not
+// miss in the instruction cache.
+__device__ __noinline__ float exact_value(float x, bool penalized, uint64_t count, RowParams p) {
+    return transform(x, penalized, count, p);
+}
+__device__ __forceinline__ float eval_slot(const Row& r, const uint32_t* bm, float x, uint32_t idx,
+                                           uint32_t col, uint32_t tok) {
+    bool penalized = false;
+    uint64_t count = 1;
+    if (r.pen) {
+        penalized = (bm[idx >> 5] >> (idx & 31)) & 1u;
+        if (penalized && r.freq)
+            count = (r.counts_row ? r.counts_row[col] : 0u) + extra_count(r, tok);
+    }
+    return exact_value(x, penalized, count, r.p);
+}
+
+// Lower bound of the smallest value v with exp(v - m) >= min_p, for any
+// m' >= m (sampling.cc:112-113 weights; the extension's min-p cut): m +
+// ln(min_p) less a slack that covers the rounding of v - m and of exp.
+__device__ __forceinline__ uint32_t minp_key(uint32_t mkey, const Row& r) {
+    if (mkey <= kNegInfKey) return 0;
+    const float m = key_float(mkey);
+    if (!isfinite(m)) return 0;
+    const double slack = (fabs(static_cast<double>(m)) + fabs(r.lnmp)) * 0x1p-18 + 1e-30;
+    return float_key(__double2float_rd(static_cast<double>(m) + r.lnmp - slack));
+}
+
+// ---------------------------------------------------------------- selects
+// Scan of 256 descending bins by warp 0: first bin at which the running
+// count reaches `need`.  Writes bin (or ~0u) and the count above it.
+__device__ __forceinline__ void find_bin_desc(const uint32_t* hist, uint32_t need, Ctl& c) {
+    if (threadIdx.x < 32) {
+        const uint32_t lane = threadIdx.x;
+        uint32_t s = 0;
+        for (int b = 0; b < 8; ++b) s += hist[255 - 8 * lane - b];
+        uint32_t inc = s;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= static_cast<uint32_t>(o)) inc += y;
+        }
+        const uint32_t hit = __ballot_sync(0xffffffffu, inc >= need);
+        if (lane == 0) c.bc_u32[0] = 0xffffffffu;
+        __syncwarp();
+        if (hit && lane == static_cast<uint32_t>(__ffs(hit) - 1)) {
+            uint32_t acc = inc - s;
+            for (int b = 0; b < 8; ++b) {
+                const uint32_t bin = 255 - 8 * lane - b;
+                acc += hist[bin];
+                if (acc >= need) {
+                    c.bc_u32[0] = bin;
+                    c.bc_u32[1] = acc - hist[bin];
+                    break;
+                }
+            }
+        }
+    }
+}
+
+// Warp-aggregated histogram increment: lanes that share a bin add once, so
+// skewed key distributions do not serialise on one shared-memory word.  The
+// whole warp calls it; `active` marks the lanes that count.
+__device__ __forceinline__ void hist_inc(uint32_t* hist, uint32_t bin, bool active) {
+    const uint32_t act = __ballot_sync(0xffffffffu, active);
+    if (active) {
+        const uint32_t peers = __match_any_sync(act, bin);
+        if ((threadIdx.x & 31) == static_cast<uint32_t>(__ffs(peers) - 1))
+            atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+    }
+}
+// Same with a 64-bit mass per lane: one round per distinct bin in the warp.
+__device__ __forceinline__ void hist_inc_mass(uint32_t* hist, uint64_t* hmass, uint32_t bin,
+                                              uint64_t mass, bool active) {
+    uint32_t todo = __ballot_sync(0xffffffffu, active);
+    while (todo) {
+        const uint32_t leader = __ffs(todo) - 1;
+        const uint32_t lb = __shfl_sync(0xffffffffu, bin, leader);
+        const bool mine = active && bin == lb;
+        const uint32_t m = __ballot_sync(0xffffffffu, mine);
+        uint64_t sum = mine ? mass : 0ull;
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if ((threadIdx.x & 31) == leader) {
+            atomicAdd(&hist[lb], static_cast<uint32_t>(__popc(m)));
+            atomicAdd(reinterpret_cast<unsigned long long*>(&hmass[lb]),
+                      static_cast<unsigned long long>(sum));
+        }
+        todo &= ~m;
+    }
+}
+// Appends `key` for every lane with `push` set; one atomic per warp.  The
+// whole warp calls it.  Returns true when the buffer overflowed.
+__device__ __forceinline__ bool warp_push(bool push, uint64_t key, uint64_t* buf, uint32_t cap,
+                                          uint32_t* counter) {
+    const uint32_t m = __ballot_sync(0xffffffffu, push);
+    if (!m) return false;
+    const uint32_t lane = threadIdx.x & 31, leader = __ffs(m) - 1;
+    uint32_t base = 0;
+    if (lane == leader) base = atomicAdd(counter, static_cast<uint32_t>(__popc(m)));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    const uint32_t pos = base + __popc(m & ((1u << lane) - 1u));
+    if (push && pos < cap) buf[pos] = key;
+    return base + __popc(m) > cap;
+}
+
+// Seed threshold from the consumers' keys (one per thread, 0 = none): the
+// largest t on the 2^8 grid with #{keys >= t} >= k, a lower bound of the
+// k-th largest key (0 when k is 0 or above 256 or fewer than k keys exist);
+// *mx gets the largest key.  Warp 0 searches bit by bit with warp sums; no
+// shared-memory atomics.
+__device__ uint32_t seed_select(uint32_t key, uint32_t k, uint32_t* mx, Ctl& c) {
+    cbar();
+    c.tkey[threadIdx.x] = key;
+    cbar();
+    if (threadIdx.x < 32) {
+        const uint32_t lane = threadIdx.x;
+        uint32_t kk[kCons / 32];
+        uint32_t m = 0;
+#pragma unroll
+        for (int i = 0; i < kCons / 32; ++i) {
+            kk[i] = c.tkey[lane + 32 * i];
+            m = max(m, kk[i]);
+        }
+        m = __reduce_max_sync(0xffffffffu, m);
+        uint32_t t = 0;
+        if (k >= 1 && k <= static_cast<uint32_t>(kCons)) {
+            for (int b = 31; b >= 8; --b) {
+                const uint32_t cand = t | (1u << b);
+                uint32_t cnt = 0;
+#pragma unroll
+                for (int i = 0; i < kCons / 32; ++i) cnt += kk[i] >= cand;
+                if (__reduce_add_sync(0xffffffffu, cnt) >= k) t = cand;
+            }
+        }
+        if (lane == 0) {
+            c.bc_u32[0] = t;
+            c.bc_u32[1] = m;
+        }
+    }
+    cbar();
+    *mx = c.bc_u32[1];
+    return c.bc_u32[0];
+}
+
+// Exact k-th largest value key (upper 32 bits of the rank keys) among
+// keys[0..n); n >= k >= 1.
+__device__ uint32_t kth_value_key(const uint64_t* keys, uint32_t n, uint32_t k, Ctl& c) {
+    uint32_t prefix = 0, mask = 0, need = k;
+    for (int level = 0; level < 4; ++level) {
+        const int shift = 24 - 8 * level;
+        cbar();
+        c.hist[threadIdx.x] = 0;
+        cbar();
+        const uint32_t nr = (n + kCons - 1) / kCons * kCons;
+        for (uint32_t i = threadIdx.x; i < nr; i += kCons) {
+            const uint32_t vk = i < n ? static_cast<uint32_t>(keys[i] >> 32) : 0u;
+            hist_inc(c.hist, (vk >> shift) & 255u, i < n && (vk & mask) == prefix);
+        }
+        cbar();
+        find_bin_desc(c.hist, need, c);
+        cbar();
+        const uint32_t bin = c.bc_u32[0];
+        if (bin == 0xffffffffu) return 0;
+        need -= c.bc_u32[1];
+        prefix |= bin << shift;
+        mask |= 255u << shift;
+    }
+    return prefix;
+}
+
+// Keeps the keys whose value key is >= vk (order not kept); n <= kBuf.
+__device__ uint32_t compact_ge(uint64_t* keys, uint32_t n, uint32_t vk, Ctl& c) {
+    constexpr uint32_t kPer = kBuf / kCons;
+    uint64_t mine[kPer];
+    uint32_t cnt = 0;
+#pragma unroll
+    for (uint32_t u = 0; u < kPer; ++u) {
+        const uint32_t i = threadIdx.x + u * kCons;
+        mine[u] = i < n ? keys[i] : 0ull;
+        cnt += (i < n && static_cast<uint32_t>(mine[u] >> 32) >= vk) ? 1u : 0u;
+    }
+    uint32_t total;
+    uint32_t pos = cscan_excl(cnt, &total, c);  // barriers: every read above is done
+#pragma unroll
+    for (uint32_t u = 0; u < kPer; ++u) {
+        const uint32_t i = threadIdx.x + u * kCons;
+        if (i < n && static_cast<uint32_t>(mine[u] >> 32) >= vk) keys[pos++] = mine[u];
+    }
+    cbar();
+    return total;
+}
+
+// keys[0..n) (distinct) sorted descending into out[0..n); n <= kGather.
+// `out` must have room for the next power of two of n when n > 128.
+__device__ void sort_desc(const uint64_t* keys, uint32_t n, uint64_t* out) {
+    if (n <= 128) {  // rank by counting
+        for (uint32_t i = threadIdx.x; i < n; i += kCons) {
+            const uint64_t x = keys[i];
+            uint32_t rank = 0;
+            for (uint32_t j = 0; j < n; ++j) rank += keys[j] > x;
+            out[rank] = x;
+        }
+        cbar();
+        return;
+    }
+    uint32_t p2 = 1;
+    while (p2 < n) p2 <<= 1;
+    for (uint32_t i = threadIdx.x; i < p2; i += kCons) out[i] = i < n ? keys[i] : 0ull;
+    cbar();
+    for (uint32_t size = 2; size <= p2; size <<= 1) {
+        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+            for (uint32_t i = threadIdx.x; i < p2 / 2; i += kCons) {
+                const uint32_t lo = 2 * i - (i & (stride - 1));
+                const uint32_t hi = lo + stride;
+                const bool desc = (lo & size) == 0;
+                const uint64_t x = out[lo], y = out[hi];
+                if ((x < y) == desc) {
+                    out[lo] = y;
+                    out[hi] = x;
+                }
+            }
+            cbar();
+        }
+    }
+}
+
+// Exact top-k / min-p cuts of the candidate buffer, then the sorted prefix
+// into `sorted`.  Returns the number kept, or ~0u when more than kFinal
+// candidates survive the cuts.
+__device__ uint32_t finish_buffer(uint64_t* cand, uint32_t n, const Row& r, uint64_t* sorted,
+                                  Ctl& c) {
+    if (n <= static_cast<uint32_t>(kCons)) {
+        // exact sort by rank counting (rank keys are distinct), then the
+        // top-k and min-p cuts are prefix lengths
+        if (threadIdx.x < n) {
+            const uint64_t x = cand[threadIdx.x];
+            uint32_t rank = 0;
+            for (uint32_t j = 0; j < n; ++j) rank += cand[j] > x;
+            sorted[rank] = x;
+        }
+        cbar();
+        uint32_t keep = r.k_eff ? min(n, r.k_eff) : n;
+        if (r.minp && keep) {
+            const float M = rank_value(sorted[0]);
+            if (isfinite(M)) {
+                const double floor_w = static_cast<double>(r.p.min_p);
+                uint32_t first = keep;
+                if (threadIdx.x < keep &&
+                    !(exp(static_cast<double>(__fsub_rn(rank_value(sorted[threadIdx.x]), M))) >=
+                      floor_w))
+                    first = threadIdx.x;
+                keep = cmin_u32(first, c);
+            }
+        }
+        return keep;
+    }
+    uint32_t vk = 0;
+    if (r.k_eff && n > r.k_eff) vk = kth_value_key(cand, n, r.k_eff, c);
+    if (r.minp && n) {
+        // exact min-p against the candidates' maximum (the row maximum, or
+        // the segment maximum for a segment's list): keep w >= min_p
+        uint32_t mk = 0;
+        for (uint32_t i = threadIdx.x; i < n; i += kCons)
+            mk = max(mk, static_cast<uint32_t>(cand[i] >> 32));
+        mk = cmax_u32(mk, c);
+        const float M = key_float(mk);
+        if (mk > kNegInfKey && isfinite(M)) {
+            const double floor_w = static_cast<double>(r.p.min_p);
+            uint32_t lowest = 0xffffffffu;
+            for (uint32_t i = threadIdx.x; i < n; i += kCons) {
+                const uint32_t k = static_cast<uint32_t>(cand[i] >> 32);
+                if (exp(static_cast<double>(__fsub_rn(key_float(k), M))) >= floor_w)
+                    lowest = min(lowest, k);
+            }
+            lowest = cmin_u32(lowest, c);
+            if (lowest != 0xffffffffu) vk = max(vk, lowest);
+        }
+    }
+    if (vk) n = compact_ge(cand, n, vk, c);
+    if (n > kFinal) return 0xffffffffu;
+    sort_desc(cand, n, sorted);
+    return r.k_eff ? min(n, r.k_eff) : n;
+}
+
+// ------------------------------------------------------ warp candidate slices
+// Exact k-th largest value key among a warp's slice entries (kWarpPer per
+// lane, 0 = empty): the largest t with #{value keys >= t} >= k, found bit by
+// bit with warp sums.  Whole warp.
+__device__ __forceinline__ uint32_t warp_kth_value(const uint64_t (&e)[kWarpPer], uint32_t k) {
+    uint32_t t = 0;
+#pragma unroll 1
+    for (int b = 31; b >= 0; --b) {
+        const uint32_t cand = t | (1u << b);
+        uint32_t cnt = 0;
+#pragma unroll
+        for (int m = 0; m < kWarpPer; ++m) cnt += static_cast<uint32_t>(e[m] >> 32) >= cand;
+        if (__reduce_add_sync(0xffffffffu, cnt) >= k) t = cand;
+    }
+    return t;
+}
+
+// A warp's slice entries (kWarpPer per lane, 0 = empty) into registers.
+__device__ __forceinline__ void load_slice(const uint64_t* slice, uint32_t cnt,
+                                           uint64_t (&e)[kWarpPer]) {
+    const uint32_t lane = threadIdx.x & 31;
+#pragma unroll
+    for (int m = 0; m < kWarpPer; ++m) {
+        const uint32_t i = lane + 32 * m;
+        e[m] = i < cnt ? slice[i] : 0ull;
+    }
+}
+
+// Exact k-th largest value key of a warp's slice (cnt > k).  The k-th
+// largest of a subset of the row is at most the row's k-th largest, so it
+// is a valid threshold.  Whole warp.
+__device__ __noinline__ uint32_t slice_kth(const uint64_t* slice, uint32_t cnt, uint32_t k) {
+    uint64_t e[kWarpPer];
+    load_slice(slice, cnt, e);
+    return warp_kth_value(e, k);
+}
+
+// Keeps the slice entries whose value key is >= th; returns the new length.
+// Whole warp.
+__device__ __noinline__ uint32_t slice_compact(uint64_t* slice, uint32_t cnt, uint32_t th) {
+    const uint32_t lane = threadIdx.x & 31;
+    uint64_t e[kWarpPer];
+    load_slice(slice, cnt, e);
+    __syncwarp();
+    uint32_t out = 0;
+#pragma unroll
+    for (int m = 0; m < kWarpPer; ++m) {
+        const bool keep = e[m] != 0ull && static_cast<uint32_t>(e[m] >> 32) >= th;
+        const uint32_t mask = __ballot_sync(0xffffffffu, keep);
+        if (keep) slice[out + __popc(mask & ((1u << lane) - 1u))] = e[m];
+        out += __popc(mask);
+    }
+    __syncwarp();
+    return out;
+}
+
+// ---------------------------------------------------------------- epilogue
+// Softmax / min-p / top-p / draw over n candidates sorted by rank key, in
+// the order of sampling.cc:105-145: w_i = exp((double)(v_i - v_0)) with the
+// difference in float, sequential double prefix sums, the quotient-
+// accumulating top-p loop (top_p widened from float), total over the
+// retained prefix, draw = uniform01(rng_before + gamma) * total, first
+// prefix sum above the draw.  min-p keeps the prefix with w_i >= min_p.
+// Warp 0 runs it (lane 0 does the sequential sums); results in c.e_*.
+__device__ void epilogue(const uint64_t* sorted, uint32_t n, const RowParams& p, bool minp,
+                         uint64_t rng_before, double* w, double* S, double* q, Ctl& c) {
+    if (threadIdx.x < 32) {
+        constexpr unsigned kFull = 0xffffffffu;
+        const uint32_t lane = threadIdx.x;
+        int32_t status = Q38S_ROW_OK, token = -1;
+        uint32_t r = 0;
+        double total = 0.0, draw = 0.0;
+        if (n == 0 || !isfinite(rank_value(sorted[0]))) {
+            status = Q38S_ROW_NO_FINITE;
+        } else {
+            const float vmax = rank_value(sorted[0]);
+            for (uint32_t i = lane; i < n; i += 32)
+                w[i] = exp(static_cast<double>(__fsub_rn(rank_value(sorted[i]), vmax)));
+            __syncwarp();
+            if (minp && p.min_p > 0.0f) {
+                const double floor_w = static_cast<double>(p.min_p);
+                uint32_t m = n;
+                for (uint32_t i0 = 0; i0 < n; i0 += 32) {
+                    const uint32_t i = i0 + lane;
+                    const uint32_t b = __ballot_sync(kFull, i < n && !(w[i] >= floor_w));
+                    if (b) {
+                        m = i0 + __ffs(b) - 1;
+                        break;
+                    }
+                }
+                n = m;
+            }
+            if (lane == 0) {
+                double acc = 0.0;
+                for (uint32_t i = 0; i < n; ++i) {
+                    acc += w[i];
+                    S[i] = acc;
+                }
+                total = acc;
+            }
+            total = __shfl_sync(kFull, total, 0);
+            if (!(total > 0.0) || !isfinite(total)) {
+                status = Q38S_ROW_NORMALIZATION;
+            } else {
+                r = n;
+                if (p.top_p < 1.0f) {
+                    for (uint32_t i = lane; i < n; i += 32) q[i] = w[i] / total;
+                    __syncwarp();
+                    uint32_t k = 0;
+                    if (lane == 0) {
+                        const double top_p = static_cast<double>(p.top_p);
+                        double cum = 0.0;
+                        while (k < n) {
+                            cum += q[k];
+                            ++k;
+                            if (cum >= top_p) break;
+                        }
+                    }
+                    r = __shfl_sync(kFull, k, 0);
+                }
+                __syncwarp();
+                total = S[r - 1];  // the sequential sum over the retained prefix
+                draw = uniform01(rng_before + kGamma) * total;
+                uint32_t sel = r - 1;
+                for (uint32_t i0 = 0; i0 < r; i0 += 32) {
+                    const uint32_t i = i0 + lane;
+                    const uint32_t b = __ballot_sync(kFull, i < r && draw < S[i]);
+                    if (b) {
+                        sel = i0 + __ffs(b) - 1;
+                        break;
+                    }
+                }
+                token = static_cast<int32_t>(rank_token(sorted[sel]));
+            }
+        }
+        if (lane == 0) {
+            c.e_status = status;
+            c.e_token = token;
+            c.e_n = n;
+            c.e_r = r;
+            c.e_total = total;
+            c.e_draw = draw;
+        }
+    }
+    cbar();
+}
+
+// ---------------------------------------------------------------- outputs
+__device__ void write_decision(const SampleArgs& a, const Row& r, int32_t token, int32_t status) {
+    if (threadIdx.x != 0) return;
+    q38s_decision_v1 d;
+    d.token = status == Q38S_ROW_OK ? token : -1;
+    d.status = status;
+    d.rng_before = r.rng_before;
+    d.rng_after = r.rng_before + kGamma;
+    if (a.decisions) a.decisions[r.v] = d;
+    if (a.mode == kModeSampleCommit && status == Q38S_ROW_OK) {
+        // commit (sampling.cc:148-156) then commit_token (sampling.cc:163-172)
+        RowState& s = a.state[r.srow];
+        s.rng_state = d.rng_after;
+        s.sampled_tokens += 1;
+        const uint32_t col = static_cast<uint32_t>(token) - a.col_begin;
+        atomicOr(&a.bitmap[static_cast<size_t>(r.srow) * a.bitmap_words + (col >> 5)],
+                 1u << (col & 31));
+        if (a.counts) atomicAdd(&a.counts[static_cast<size_t>(r.srow) * a.vocab + col], 1u);
+        s.canonical_tokens += 1;
+        s.penalty_checksum ^= splitmix64(static_cast<uint64_t>(static_cast<uint32_t>(token)) ^
+                                         (s.canonical_tokens * kGamma));
+    }
+}
+
+__device__ void write_distribution(const SampleArgs& a, const Row& r, const uint64_t* sorted,
+                                   const double* w, Ctl& c) {
+    if (a.dist.capacity == 0) return;
+    const uint32_t cap = a.dist.capacity;
+    const size_t base = static_cast<size_t>(r.v) * cap;
+    const bool ok = c.e_status == Q38S_ROW_OK;
+    const uint32_t n = ok ? c.e_n : 0;
+    const uint32_t rr = ok ? c.e_r : 0;
+    for (uint32_t i = threadIdx.x; i < min(n, cap); i += kCons) {
+        if (a.dist.tokens) a.dist.tokens[base + i] = static_cast<int32_t>(rank_token(sorted[i]));
+        if (a.dist.values) a.dist.values[base + i] = rank_value(sorted[i]);
+        if (a.dist.probs) a.dist.probs[base + i] = i < rr ? w[i] / c.e_total : 0.0;
+    }
+    if (threadIdx.x == 0) {
+        if (a.dist.n_candidates) a.dist.n_candidates[r.v] = n;
+        if (a.dist.n_retained) a.dist.n_retained[r.v] = rr;
+        if (a.dist.total) a.dist.total[r.v] = c.e_total;
+        if (a.dist.draw) a.dist.draw[r.v] = c.e_draw;
+    }
+}
+
+__device__ void row_error(const SampleArgs& a, const Row& r, int32_t status) {
+    if (a.mode == kModeShardTopK) {
+        for (uint32_t i = threadIdx.x; i < a.k_out; i += kCons) {
+            q38s_candidate cd;
+            cd.value = -INFINITY;
+            cd.token = -1;
+            a.topk_out[static_cast<size_t>(r.v) * a.k_out + i] = cd;
+        }
+        return;
+    }
+    write_decision(a, r, -1, status);
+    if (a.dist.capacity && threadIdx.x == 0) {
+        if (a.dist.n_candidates) a.dist.n_candidates[r.v] = 0;
+        if (a.dist.n_retained) a.dist.n_retained[r.v] = 0;
+    }
+}
+
+// Final outputs of a row from its sorted candidate list.
+__device__ void row_output(const SampleArgs& a, const Row& r, const uint64_t* sorted,
+                           uint32_t keep, double* w, double* S, double* q, Ctl& c) {
+    if (a.mode == kModeShardTopK) {
+        for (uint32_t i = threadIdx.x; i < a.k_out; i += kCons) {
+            q38s_candidate cd;
+            if (i < keep) {
+                cd.value = rank_value(sorted[i]);
+                cd.token = static_cast<int32_t>(rank_token(sorted[i]));
+            } else {
+                cd.value = -INFINITY;
+                cd.token = -1;
+            }
+            a.topk_out[static_cast<size_t>(r.v) * a.k_out + i] = cd;
+        }
+        return;
+    }
+    epilogue(sorted, keep, r.p, r.minp, r.rng_before, w, S, q, c);
+    write_decision(a, r, c.e_token, c.e_status);
+    write_distribution(a, r, sorted, w, c);
+}
+
+// Speculative verification over all virtual rows' distributions (target
+// rows 0..n, draft rows n+1..2n); one thread of the CTA that finished the
+// last row.  Leviathan et al. 2023 / Chen et al. 2023 rejection sampling:
+// draft i is accepted iff u_i * q_i(d_i) < p_i(d_i) with u_i =
+// uniform01(s_i ^ kAcceptDomain), s_i = rng_state + (i + 1) * gamma; the
+// first rejection draws from max(0, p_i - q_i) over p_i's sorted support
+// with uniform01(s_i); if every draft is accepted the bonus token is the
+// reference draw from p_n.  Other CTAs wrote these arrays: L2 loads.
+__device__ void mtp_finish(const SampleArgs& a) {
+    q38s_mtp_result res;
+    const uint32_t n = a.n_draft;
+    const uint32_t cap = a.dist.capacity;
+    const uint64_t rng0 = __ldcg(reinterpret_cast<const unsigned long long*>(
+        &a.state[a.vrow_state_const].rng_state));
+    res.rng_before = rng0;
+    res.status = Q38S_ROW_OK;
+    res.n_tokens = 0;
+    res.n_accepted = 0;
+    for (uint32_t i = 0; i <= n; ++i) {
+        const int32_t t_status = __ldcg(&a.decisions[i].status);
+        const int32_t t_token = __ldcg(&a.decisions[i].token);
+        const uint64_t s_i = rng0 + (static_cast<uint64_t>(i) + 1) * kGamma;
+        if (t_status != Q38S_ROW_OK) {
+            res.status = t_status;
+            break;
+        }
+        if (i == n) {  // bonus row: the reference draw from p_n
+            res.tokens[res.n_tokens++] = t_token;
+            break;
+        }
+        const int32_t d_status = __ldcg(&a.decisions[n + 1 + i].status);
+        if (d_status != Q38S_ROW_OK) {
+            res.status = d_status;
+            break;
+        }
+        const uint32_t np = __ldcg(&a.dist.n_retained[i]);
+        const uint32_t nq = __ldcg(&a.dist.n_retained[n + 1 + i]);
+        if (np > cap || nq > cap || np == 0) {
+            res.status = Q38S_ROW_NORMALIZATION;
+            break;
+        }
+        const int32_t* pt = a.dist.tokens + static_cast<size_t>(i) * cap;
+        const double* pp = a.dist.probs + static_cast<size_t>(i) * cap;
+        const int32_t* qt = a.dist.tokens + static_cast<size_t>(n + 1 + i) * cap;
+        const double* qp = a.dist.probs + static_cast<size_t>(n + 1 + i) * cap;
+        const int32_t d = a.draft_tokens[i];
+        double pd = 0.0, qd = 0.0;
+        for (uint32_t j = 0; j < np; ++j)
+            if (__ldcg(&pt[j]) == d) pd = __ldcg(&pp[j]);
+        for (uint32_t j = 0; j < nq; ++j)
+            if (__ldcg(&qt[j]) == d) qd = __ldcg(&qp[j]);
+        const double ua = uniform01(s_i ^ kAcceptDomain);
+        if (ua * qd < pd) {
+            res.tokens[res.n_tokens++] = d;
+            ++res.n_accepted;
+            continue;
+        }
+        auto q_of = [&](int32_t tok) {
+            double qj = 0.0;
+            for (uint32_t m = 0; m < nq; ++m)
+                if (__ldcg(&qt[m]) == tok) qj = __ldcg(&qp[m]);
+            return qj;
+        };
+        double rtotal = 0.0;
+        for (uint32_t j = 0; j < np; ++j) rtotal += fmax(0.0, __ldcg(&pp[j]) - q_of(__ldcg(&pt[j])));
+        int32_t tok = t_token;  // empty residual: the reference draw from p_i
+        if (rtotal > 0.0) {
+            const double draw = uniform01(s_i) * rtotal;
+            double cum = 0.0;
+            uint32_t sel = np - 1;
+            for (uint32_t j = 0; j < np; ++j) {
+                cum += fmax(0.0, __ldcg(&pp[j]) - q_of(__ldcg(&pt[j])));
+                if (draw < cum) {
+                    sel = j;
+                    break;
+                }
+            }
+            tok = __ldcg(&pt[sel]);
+        }
+        res.tokens[res.n_tokens++] = tok;
+        break;
+    }
+    res.rng_after = res.rng_before + static_cast<uint64_t>(res.n_tokens) * kGamma;
+    *a.mtp = res;
+}
+
+// A virtual row is complete: the last one runs the speculative verification.
+__device__ void row_done(const SampleArgs& a, Ctl& c) {
+    if (!a.mtp) return;
+    __threadfence();
+    cbar();
+    if (threadIdx.x == 0) c.bc_u32[2] = atomicAdd(a.ticket, 1u) == a.vrows - 1;
+    cbar();
+    if (c.bc_u32[2] && threadIdx.x == 0) {
+        __threadfence();
+        *a.ticket = 0;
+        mtp_finish(a);
+    }
+}
+
+// ------------------------------------------------------------ general path
+struct Cut {
+    uint32_t M_key;
+    float M;
+    uint32_t minp_key;
+    bool has_cut;
+    uint32_t cut_key;
+    uint32_t cut_tok;
+};
+
+__device__ __forceinline__ bool in_k0(const Cut& g, uint32_t key, uint32_t tok) {
+    if (key < g.minp_key) return false;
+    if (!g.has_cut) return true;
+    return key > g.cut_key || (key == g.cut_key && tok <= g.cut_tok);
+}
+__device__ __forceinline__ uint64_t wfix(const Cut& g, uint32_t key) {
+    const double w = exp(static_cast<double>(__fsub_rn(key_float(key), g.M)));
+    return static_cast<uint64_t>(w * kFix + 0.5);
+}
+
+struct Sel {
+    bool found;
+    uint32_t key;
+    uint32_t token;
+    uint64_t through;  // count or fixed-point mass up to and including the element
+};
+
+// Radix selection over the row's exact keys (global scratch, one per
+// column) restricted to K0 (or to key >= minp_key when !restrict_k0): the
+// first element in canonical order (value desc, token asc) at which the
+// running count (weighted = false) or fixed-point mass (weighted = true)
+// reaches tau (>= tau, or > tau when strict).
+__device__ Sel row_select(const uint32_t* keys, uint32_t V, uint32_t tok0, const Cut& g0,
+                          bool restrict_k0, bool weighted, uint64_t tau, bool strict, Ctl& c) {
+    Cut g = g0;
+    if (!restrict_k0) g.has_cut = false;
+    uint32_t prefix = 0, mask = 0;
+    uint64_t above = 0;
+    Sel res{false, 0, 0, 0};
+    uint32_t group = 0;
+    for (int level = 0; level < 4; ++level) {
+        const int shift = 24 - 8 * level;
+        cbar();
+        c.hist[threadIdx.x] = 0;
+        c.hmass[threadIdx.x] = 0;
+        cbar();
+        const uint32_t Vr = (V + kCons - 1) / kCons * kCons;
+        for (uint32_t j = threadIdx.x; j < Vr; j += kCons) {
+            const uint32_t key = j < V ? keys[j] : 0u;
+            const bool act = j < V && (key & mask) == prefix && in_k0(g, key, tok0 + j);
+            const uint32_t d = (key >> shift) & 255u;
+            if (weighted) hist_inc_mass(c.hist, c.hmass, d, act ? wfix(g, key) : 0ull, act);
+            else hist_inc(c.hist, d, act);
+        }
+        cbar();
+        if (threadIdx.x == 0) {
+            uint64_t acc = above;
+            int hit = -1;
+            for (int d = 255; d >= 0; --d) {
+                if (c.hist[d] == 0) continue;
+                const uint64_t nxt = acc + (weighted ? c.hmass[d] : c.hist[d]);
+                if (strict ? (nxt > tau) : (nxt >= tau)) {
+                    hit = d;
+                    break;
+                }
+                acc = nxt;
+            }
+            c.bc_u32[0] = static_cast<uint32_t>(hit);
+            c.bc_u32[1] = hit >= 0 ? c.hist[hit] : 0u;
+            c.bc_u64[0] = acc;
+        }
+        cbar();
+        const int hit = static_cast<int>(c.bc_u32[0]);
+        if (hit < 0) return res;
+        group = c.bc_u32[1];
+        above = c.bc_u64[0];
+        prefix |= static_cast<uint32_t>(hit) << shift;
+        mask |= 255u << shift;
+    }
+    // position j inside the tie group {key == prefix} (token order)
+    const uint32_t key = prefix;
+    uint64_t j, per = 1;
+    if (weighted) {
+        per = wfix(g, key);
+        if (per == 0) {
+            j = 0;
+        } else if (strict) {
+            j = (tau - above) / per;
+        } else {
+            const uint64_t need = tau > above ? tau - above : 0;
+            j = need == 0 ? 0 : (need + per - 1) / per - 1;
+        }
+    } else {
+        j = tau > above ? tau - above - 1 : 0;
+    }
+    if (j >= group) j = group - 1;
+    // the j-th smallest token of the group: radix over the token bits
+    uint32_t tprefix = 0, tmask = 0, need = static_cast<uint32_t>(j);
+    for (int level = 0; level < 4; ++level) {
+        const int shift = 24 - 8 * level;
+        cbar();
+        c.hist[threadIdx.x] = 0;
+        cbar();
+        const uint32_t Vr = (V + kCons - 1) / kCons * kCons;
+        for (uint32_t x = threadIdx.x; x < Vr; x += kCons) {
+            const uint32_t tok = tok0 + x;
+            const bool act =
+                x < V && keys[x] == key && (tok & tmask) == tprefix && in_k0(g, key, tok);
+            hist_inc(c.hist, (tok >> shift) & 255u, act);
+        }
+        cbar();
+        if (threadIdx.x == 0) {
+            uint32_t left = need, d = 0;
+            for (; d < 255; ++d) {
+                if (left < c.hist[d]) break;
+                left -= c.hist[d];
+            }
+            c.bc_u32[0] = d;
+            c.bc_u32[1] = left;
+        }
+        cbar();
+        tprefix |= c.bc_u32[0] << shift;
+        tmask |= 255u << shift;
+        need = c.bc_u32[1];
+    }
+    res.found = true;
+    res.key = key;
+    res.token = tprefix;
+    res.through = above + (j + 1) * per;
+    return res;
+}
+
+template <int DT>
+__device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* area, Ctl& c) {
+    const uint32_t V = a.vocab;
+    const uint32_t tok0 = a.col_begin;
+    uint32_t* keys = a.scratch + static_cast<size_t>(r.v) * V;
+    const unsigned char* row = row_ptr<DT>(a, r.v);
+    // this call's penalised columns in shared memory when they fit
+    const uint32_t words = (V + 31) / 32;
+    const uint32_t* pbm = nullptr;
+    if (r.pen && words * 4 <= kArea) {
+        uint32_t* sbm = reinterpret_cast<uint32_t*>(area);
+        cbar();
+        for (uint32_t i = threadIdx.x; i < words; i += kCons) sbm[i] = r.gbm[i];
+        cbar();
+        for (uint32_t e = threadIdx.x; e < r.n_extra; e += kCons) {
+            const uint32_t col = static_cast<uint32_t>(r.extra[e]) - tok0;
+            if (col < V) atomicOr(&sbm[col >> 5], 1u << (col & 31));
+        }
+        cbar();
+        pbm = sbm;
+    }
+    // G0: exact key of every column
+    uint32_t kmax = 0;
+    for (uint32_t j = threadIdx.x; j < V; j += kCons) {
+        const float x = load_elem<DT>(row, j);
+        bool penalized = false;
+        uint64_t count = 1;
+        if (r.pen) {
+            if (pbm) {
+                penalized = (pbm[j >> 5] >> (j & 31)) & 1u;
+                if (penalized && r.freq)
+                    count = (r.counts_row ? r.counts_row[j] : 0u) + extra_count(r, tok0 + j);
+            } else {
+                const uint64_t ex = extra_count(r, tok0 + j);
+                penalized = ((r.gbm[j >> 5] >> (j & 31)) & 1u) || ex;
+                if (penalized && r.freq) count = (r.counts_row ? r.counts_row[j] : 0u) + ex;
+            }
+        }
+        const uint32_t k = float_key(transform(x, penalized, count, r.p));
+        keys[j] = k;
+        kmax = max(kmax, k);
+    }
+    Cut g;
+    g.M_key = cmax_u32(kmax, c);  // its barriers also publish keys[] to the CTA
+    g.M = key_float(g.M_key);
+    g.has_cut = false;
+    g.cut_key = 0;
+    g.cut_tok = 0;
+    g.minp_key = 0;
+    if (a.mode != kModeShardTopK && (g.M_key <= kNegInfKey || isinf(g.M))) {
+        row_error(a, r, Q38S_ROW_NO_FINITE);
+        return;
+    }
+    // G1: smallest key whose weight reaches min_p
+    if (r.minp) {
+        if (threadIdx.x == 0) {
+            const double floor_w = static_cast<double>(r.p.min_p);
+            uint32_t lo = kNegInfKey, hi = g.M_key;  // weight(M) = 1 >= min_p
+            while (lo < hi) {
+                const uint32_t mid = lo + (hi - lo) / 2;
+                const double w = exp(static_cast<double>(__fsub_rn(key_float(mid), g.M)));
+                if (w >= floor_w) hi = mid;
+                else lo = mid + 1;
+            }
+            c.bc_u32[3] = hi;
+        }
+        cbar();
+        g.minp_key = c.bc_u32[3];
+    }
+    // G2: the kept set K0 = top-k of {key >= minp_key}
+    uint32_t cnt = 0;
+    for (uint32_t j = threadIdx.x; j < V; j += kCons) cnt += keys[j] >= g.minp_key;
+    const uint32_t c_minp = csum_u32(cnt, c);
+    const uint32_t n0 = r.k_eff ? min(r.k_eff, c_minp) : c_minp;
+    if (n0 < c_minp) {
+        const Sel cut = row_select(keys, V, tok0, g, false, false, n0, false, c);
+        g.has_cut = true;
+        g.cut_key = cut.key;
+        g.cut_tok = cut.token;
+    }
+    if (n0 <= kGather) {
+        // G3: gather K0, sort, finish exactly
+        uint64_t* gk = reinterpret_cast<uint64_t*>(area + kGather * 8);  // unsorted
+        uint64_t* lk = reinterpret_cast<uint64_t*>(area);                 // sorted
+        cbar();
+        if (threadIdx.x == 0) c.bc_u32[2] = 0;
+        cbar();
+        const uint32_t Vr = (V + kCons - 1) / kCons * kCons;
+        for (uint32_t j = threadIdx.x; j < Vr; j += kCons) {
+            const uint32_t k = j < V ? keys[j] : 0u;
+            const bool act = j < V && in_k0(g, k, tok0 + j);
+            warp_push(act, rank_key(k, tok0 + j), gk, kGather, &c.bc_u32[2]);
+        }
+        cbar();
+        const uint32_t m = min(c.bc_u32[2], kGather);
+        sort_desc(gk, m, lk);
+        double* w = reinterpret_cast<double*>(area + kGather * 8);
+        double* S = reinterpret_cast<double*>(area + kGather * 16);
+        double* q = reinterpret_cast<double*>(area + kGather * 24);
+        row_output(a, r, lk, m, w, S, q, c);
+        return;
+    }
+    // G4: large kept set: fixed-point masses (2^-43 units) locate the top-p
+    // cut and the draw
+    uint64_t part = 0;
+    for (uint32_t j = threadIdx.x; j < V; j += kCons) {
+        const uint32_t k = keys[j];
+        if (in_k0(g, k, tok0 + j)) part += wfix(g, k);
+    }
+    const uint64_t Z = csum_u64(part, c);
+    int32_t status = Q38S_ROW_OK;
+    int32_t token = -1;
+    uint64_t Zr = Z;
+    Sel cutp{false, 0, 0, 0};
+    if (Z == 0) status = Q38S_ROW_NORMALIZATION;
+    if (status == Q38S_ROW_OK && r.p.top_p < 1.0f) {
+        const uint64_t tau = static_cast<uint64_t>(static_cast<double>(r.p.top_p) *
+                                                   static_cast<double>(Z));
+        cutp = row_select(keys, V, tok0, g, true, true, tau, false, c);
+        if (cutp.found) Zr = cutp.through;
+    }
+    double draw_d = 0.0;
+    if (status == Q38S_ROW_OK) {
+        const double u = uniform01(r.rng_before + kGamma);
+        const uint64_t draw = static_cast<uint64_t>(u * static_cast<double>(Zr));
+        draw_d = static_cast<double>(draw) / kFix;
+        const Sel sel = row_select(keys, V, tok0, g, true, true, draw, true, c);
+        if (sel.found) token = static_cast<int32_t>(sel.token);
+        else if (cutp.found) token = static_cast<int32_t>(cutp.token);
+        else status = Q38S_ROW_NORMALIZATION;
+    }
+    write_decision(a, r, token, status);
+    if (a.dist.capacity && threadIdx.x == 0) {
+        if (a.dist.n_candidates) a.dist.n_candidates[r.v] = n0;
+        if (a.dist.n_retained) a.dist.n_retained[r.v] = 0xffffffffu;
+        if (a.dist.total) a.dist.total[r.v] = static_cast<double>(Zr) / kFix;
+        if (a.dist.draw) a.dist.draw[r.v] = draw_d;
+    }
+}
+
+// Completes a row once its candidate list (or failure) is known.
+template <int DT>
+__device__ void finish_row(const SampleArgs& a, const Row& r, uint32_t flags,
+                           const uint64_t* sorted, uint32_t keep, unsigned char* area, Ctl& c) {
+    if (flags & kFTimeout) {
+        row_error(a, r, Q38S_ROW_TIMEOUT);
+    } else if (flags & kFInf) {
+        row_error(a, r, Q38S_ROW_NO_FINITE);
+    } else if (flags & kFOverflow) {
+        general_row<DT>(a, r, area, c);
+    } else {
+        double* w = reinterpret_cast<double*>(area + (kBuf + kFinal) * 8);
+        row_output(a, r, sorted, keep, w, w + kFinal, w + 2 * kFinal, c);
+    }
+    row_done(a, c);
+}
+
+// ------------------------------------------------------------ the kernel
+__device__ __forceinline__ void chunk_range(uint32_t vocab, uint32_t S, uint32_t seg, uint32_t& lo,
+                                            uint32_t& hi) {
+    const uint32_t nblk = (vocab + 127) / 128;
+    const uint32_t b0 = static_cast<uint32_t>((static_cast<uint64_t>(nblk) * seg) / S);
+    const uint32_t b1 = static_cast<uint32_t>((static_cast<uint64_t>(nblk) * (seg + 1)) / S);
+    lo = min(b0 * 128u, vocab);
+    hi = min(b1 * 128u, vocab);
+}
+
+__device__ bool wait_full(Ctl& c, uint32_t slot, uint32_t phase) {
+    const long long start = clock64();
+    while (!mbar_try_wait(&c.full[slot], phase)) {
+        if (*reinterpret_cast<volatile uint32_t*>(&c.abort_flag)) return false;
+        if (clock64() - start > kWaitLimitCycles) return false;
+    }
+    return true;
+}
+
+// Producer: one lane streams every tile of the CTA's units, in the order
+// the consumers read them.
+template <int DT>
+__device__ void produce(const SampleArgs& a, unsigned char* ring, Ctl& c) {
+    constexpr uint32_t es = DT == Q38S_DTYPE_BF16 ? 2u : 4u;
+    constexpr uint32_t TC = kTileBytes / es;
+    const uint32_t S = a.segs;
+    const uint32_t n_units = a.vrows * S;
+    uint32_t g = 0;
+    for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const uint32_t v = u / S;
+        uint32_t c0, c1;
+        chunk_range(a.vocab, S, u % S, c0, c1);
+        const uint32_t srow = state_row(a, v);
+        const bool pen = (a.params[srow].flags & kFlagPenalties) != 0;
+        const unsigned char* row = row_ptr<DT>(a, v);
+        const uint32_t* bmrow = a.bitmap + static_cast<size_t>(srow) * a.bitmap_words;
+        for (uint32_t t0 = c0; t0 < c1; t0 += TC, ++g) {
+            const uint32_t slot = g % kRing;
+            if (g >= kRing) {
+                const long long start = clock64();
+                while (!mbar_try_wait(&c.empty[slot], ((g / kRing) - 1) & 1u)) {
+                    if (*reinterpret_cast<volatile uint32_t*>(&c.abort_flag) ||
+                        clock64() - start > kWaitLimitCycles) {
+                        atomicOr(&c.abort_flag, 1u);
+                        atomicExch(&c.prod_done, 1u);
+                        return;
+                    }
+                }
+            }
+            if (*reinterpret_cast<volatile uint32_t*>(&c.abort_flag)) {
+                atomicExch(&c.prod_done, 1u);
+                return;
+            }
+            const uint32_t n = min(c1 - t0, TC);
+            const uint32_t bytes = n * es;
+            const uint32_t bulk = a.use_tma ? (bytes & ~15u) : 0u;
+            const uint32_t bmb = pen ? ((n + 127) / 128) * 16 : 0u;
+            unsigned char* sl = ring + slot * kSlot;
+            mbar_arrive_expect_tx(&c.full[slot], bulk + bmb);
+            if (bulk) tma_load_1d(sl, row + static_cast<size_t>(t0) * es, bulk, &c.full[slot]);
+            if (bmb) tma_load_1d(sl + kTileBytes, bmrow + t0 / 32, bmb, &c.full[slot]);
+            atomicExch(&c.issued, g + 1);
+        }
+    }
+    atomicExch(&c.prod_done, 1u);
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
+    extern __shared__ __align__(1024) unsigned char dsm[];
+    __shared__ Ctl c;
+    constexpr uint32_t es = DT == Q38S_DTYPE_BF16 ? 2u : 4u;
+    constexpr uint32_t pv = 16u / es;  // elements per 16-byte vector
+    constexpr uint32_t TC = kTileBytes / es;
+    constexpr int kU = kTileBytes / 16 / kCons;  // vectors per thread per tile
+    constexpr unsigned kFull = 0xffffffffu;
+    unsigned char* ring = dsm;
+    unsigned char* area = dsm + kRing * kSlot;
+    uint64_t* cand = reinterpret_cast<uint64_t*>(area);
+    uint64_t* sorted = cand + kBuf;
+    const uint32_t tid = threadIdx.x;
+
+    if (tid == 0) {
+        for (uint32_t i = 0; i < kRing; ++i) {
+            mbar_init(&c.full[i], 1);
+            mbar_init(&c.empty[i], kCons / 32);  // one arrival per consumer warp
+        }
+        c.abort_flag = 0;
+        c.prod_done = 0;
+        c.issued = 0;
+        c.fail_g = 0xffffffffu;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid >= static_cast<uint32_t>(kCons)) {
+        if (tid == static_cast<uint32_t>(kCons)) produce<DT>(a, ring, c);
+        return;
+    }
+
+    // Consumers.  Inside a unit the warps run decoupled: each waits for and
+    // releases the slots itself, keeps its own threshold and pushes its
+    // candidates into its own slice of the buffer (a register counter, no
+    // shared atomics).  Block barriers: the seed (once per unit), rare tile
+    // fix-ups, and the end of the unit.
+    const uint32_t warp = tid >> 5, lane = tid & 31;
+    uint64_t* slice = cand + warp * kSlice;
+    const uint32_t S = a.segs;
+    const uint32_t n_units = a.vrows * S;
+    uint32_t g = 0;     // tiles passed (the producer's order)
+    bool stop = false;  // this warp gave up on a copy (warp-uniform)
+    for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const uint32_t v = u / S, seg = u % S;
+        uint32_t c0, c1;
+        chunk_range(a.vocab, S, seg, c0, c1);
+        const uint32_t ntiles = (c1 - c0 + TC - 1) / TC;
+        Q38S_TT(u, 0);
+        Row r;
+        load_row(a, v, r);
+        Q38S_TT(u, 1);
+        if (tid == 0) {
+            c.flags = 0;
+            c.mrun = 0;
+        }
+        cbar();
+        uint32_t theta = 0, cnt = 0, seen_m = 0;
+        bool hopeless = false, wover = false;
+        const unsigned char* src_row = row_ptr<DT>(a, v);
+        for (uint32_t t = 0; t < ntiles; ++t, ++g) {
+            const uint32_t slot = g % kRing;
+            unsigned char* sl = ring + slot * kSlot;
+            uint32_t* sbm = reinterpret_cast<uint32_t*>(sl + kTileBytes);
+            const uint32_t t0 = c0 + t * TC;
+            const uint32_t n = min(c1 - t0, TC);
+            bool ok = !stop && wait_full(c, slot, (g / kRing) & 1u);
+            ok = __all_sync(kFull, ok);
+            if (!ok && !stop) {
+                stop = true;
+                if (lane == 0) {
+                    atomicOr(&c.abort_flag, 1u);
+                    atomicMin(&c.fail_g, g);
+                }
+            }
+            // consumer-side writes into the slot: the part the bulk copy
+            // cannot move (ragged tail, unaligned rows), -inf padding to a
+            // whole vector, this call's additional penalty tokens
+            const uint32_t bytes = n * es;
+            const uint32_t bulk = a.use_tma ? (bytes & ~15u) : 0u;
+            const uint32_t padded = ((n + pv - 1) / pv) * pv;
+            const bool fix = bulk < bytes || padded != n;
+            const bool mark = r.pen && r.n_extra > 0;
+            if (fix || mark) {
+                const bool all_ok = !cbar_or(!ok);
+                if (all_ok) {
+                    const unsigned char* src = src_row + static_cast<size_t>(t0) * es;
+                    for (uint32_t b = bulk + tid; b < bytes; b += kCons) sl[b] = src[b];
+                    for (uint32_t j = n + tid; j < padded; j += kCons) {
+                        if (DT == Q38S_DTYPE_BF16) reinterpret_cast<uint16_t*>(sl)[j] = 0xff80u;
+                        else reinterpret_cast<uint32_t*>(sl)[j] = 0xff800000u;
+                    }
+                    if (mark) {
+                        for (uint32_t e = tid; e < r.n_extra; e += kCons) {
+                            const uint32_t col = static_cast<uint32_t>(r.extra[e]) - a.col_begin;
+                            if (col >= t0 && col < t0 + n)
+                                atomicOr(&sbm[(col - t0) >> 5], 1u << ((col - t0) & 31));
+                        }
+                    }
+                }
+                fence_async_smem();  // generic writes before the slot's next bulk copy
+                cbar();
+            }
+            // the thread's vectors of this tile
+            const uint4* vec = reinterpret_cast<const uint4*>(sl);
+            const uint32_t nvec = padded / pv;
+            uint4 wv[kU];
+#pragma unroll
+            for (int q = 0; q < kU; ++q) {
+                const uint32_t j = tid + q * kCons;
+                wv[q] = (ok && j < nvec)
+                            ? vec[j]
+                            : (DT == Q38S_DTYPE_BF16
+                                   ? make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u)
+                                   : make_uint4(0xff800000u, 0xff800000u, 0xff800000u,
+                                                0xff800000u));
+            }
+            if (t == 0) {
+                // seed (every warp takes part): exact value of each thread's
+                // largest raw logit, then the block's k-th / maximum
+                float best = -INFINITY;
+                int bq = -1;
+#pragma unroll
+                for (int q = 0; q < kU; ++q) {
+                    const float f = vec_max<DT>(wv[q]);
+                    if (f > best) {
+                        best = f;
+                        bq = q;
+                    }
+                }
+                uint32_t tk = 0;
+                if (ok && bq >= 0) {
+                    const uint32_t j = tid + bq * kCons;
+#pragma unroll 1
+                    for (uint32_t e = 0; e < pv; ++e) {
+                        const uint32_t idx = j * pv + e;
+                        if (idx >= n) break;
+                        const float x = load_elem<DT>(sl, idx);
+                        if (x == best) {
+                            const float vx =
+                                eval_slot(r, sbm, x, idx, t0 + idx, a.col_begin + t0 + idx);
+                            if (vx == INFINITY) atomicOr(&c.flags, kFInf);
+                            tk = float_key(vx);
+                            break;
+                        }
+                    }
+                }
+                uint32_t m0;
+                theta = seed_select(tk, r.k_eff, &m0, c);
+                if (r.minp) theta = max(theta, minp_key(m0, r));
+                if (tid == 0) atomicMax(&c.mrun, m0);
+                seen_m = m0;
+                hopeless = theta <= kNegInfKey && (c1 - c0) > kBuf;
+                Q38S_TT(u, 2);
+                Q38S_TR(u, 3, (static_cast<unsigned long long>(theta) << 32) | hopeless);
+            } else if (r.minp) {
+                // the min-p bound follows the running maximum of all warps
+                const uint32_t mr = *reinterpret_cast<volatile uint32_t*>(&c.mrun);
+                if (mr > seen_m) {
+                    seen_m = mr;
+                    theta = max(theta, minp_key(mr, r));
+                }
+            }
+            if (ok && !hopeless && !wover) {
+                const float th = theta <= kNegInfKey ? -INFINITY : key_float(theta);
+                const float rho = raw_bound(th, r.p.temperature);
+                bool hit;
+                if (DT == Q38S_DTYPE_BF16) {
+                    const __nv_bfloat16 rb = __float2bfloat16_rd(rho);
+                    const __nv_bfloat162 r2 = __halves2bfloat162(rb, rb);
+                    __nv_bfloat162 m = *reinterpret_cast<const __nv_bfloat162*>(&wv[0].x);
+#pragma unroll
+                    for (int q = 0; q < kU; ++q) {
+                        m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&wv[q].x));
+                        m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&wv[q].y));
+                        m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&wv[q].z));
+                        m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&wv[q].w));
+                    }
+                    hit = !__hblt2(m, r2);
+                } else {
+                    float m = -INFINITY;
+#pragma unroll
+                    for (int q = 0; q < kU; ++q) m = fmaxf(m, vec_max<DT>(wv[q]));
+                    hit = !(m < rho);
+                }
+                // rare path: exact values of the hits into the warp's slice;
+                // rolled loops keep it small
+                if (__any_sync(kFull, hit || r.nonmono)) {
+                    const uint32_t tokt = a.col_begin + t0;
+                    uint32_t wmax = 0;
+                    bool inf = false;
+#pragma unroll 1
+                    for (int q = 0; q < kU; ++q) {
+                        const uint32_t j = tid + q * kCons;
+                        uint32_t look = 0;
+                        if (j < nvec) {
+                            const uint4 w4 = vec[j];
+                            uint32_t penbits = 0;
+                            if (r.nonmono) {
+                                const uint32_t e0 = j * pv;
+                                penbits = (sbm[e0 >> 5] >> (e0 & 31)) & ((1u << pv) - 1u);
+                            }
+#pragma unroll
+                            for (int e = 0; e < static_cast<int>(pv); ++e) {
+                                const float x = vec_elem<DT>(w4, e);
+                                if ((!(x < rho) || ((penbits >> e) & 1u)) && j * pv + e < n)
+                                    look |= 1u << e;
+                            }
+                        }
+                        while (__any_sync(kFull, look != 0)) {
+                            uint32_t k = 0, idx = 0;
+                            bool push = false;
+                            if (look) {
+                                idx = j * pv + (__ffs(look) - 1);
+                                look &= look - 1;
+                                const float vx = eval_slot(r, sbm, load_elem<DT>(sl, idx), idx,
+                                                           t0 + idx, tokt + idx);
+                                inf |= vx == INFINITY;
+                                k = float_key(vx);
+                                push = k >= theta;
+                                if (push) wmax = max(wmax, k);
+                            }
+                            const uint32_t pm = __ballot_sync(kFull, push);
+                            if (push) {
+                                const uint32_t pos = cnt + __popc(pm & ((1u << lane) - 1u));
+                                if (pos < kSlice) slice[pos] = rank_key(k, tokt + idx);
+                            }
+                            cnt += __popc(pm);
+                            if (cnt > kSlice) wover = true;
+                            if (cnt > kShrinkAt && !wover) {
+                                // warp-local compaction around the slice's k-th value
+                                if (r.k_eff && cnt > r.k_eff)
+                                    theta = max(theta, slice_kth(slice, cnt, r.k_eff));
+                                cnt = slice_compact(slice, cnt, theta);
+                                if (cnt > kShrinkAt) wover = true;
+                            }
+                        }
+                    }
+                    wmax = __reduce_max_sync(kFull, wmax);
+                    if (__any_sync(kFull, inf) && lane == 0) atomicOr(&c.flags, kFInf);
+                    if (wmax > seen_m) {
+                        seen_m = wmax;
+                        if (lane == 0) atomicMax(&c.mrun, wmax);
+                        if (r.minp) theta = max(theta, minp_key(wmax, r));
+                    }
+                }
+            }
+            __syncwarp();
+            // release the slot once every lane has read it; a slot whose
+            // wait failed is never released (its copy may still land)
+            if (ok && lane == 0) mbar_arrive(&c.empty[slot]);
+        }
+        // ---- end of unit: the warps' slices into one contiguous list
+        if (lane == 0) c.wcnt[warp] = wover ? kSlice + 1 : cnt;
+        const bool any_stop = cbar_or(stop);
+        uint32_t total = 0, my_off = 0;
+        bool over = false;
+#pragma unroll
+        for (uint32_t w2 = 0; w2 < kCons / 32; ++w2) {
+            const uint32_t cw = c.wcnt[w2];
+            over |= cw > kSlice;
+            const uint32_t len = min(cw, kSlice);
+            if (w2 < warp) my_off += len;
+            total += len;
+        }
+        if (!over && !hopeless && !any_stop) {
+            uint64_t e[kWarpPer];
+            load_slice(slice, cnt, e);
+            cbar();
+#pragma unroll
+            for (int m = 0; m < kWarpPer; ++m) {
+                const uint32_t i = lane + 32 * m;
+                if (i < cnt) cand[my_off + i] = e[m];
+            }
+        }
+        cbar();
+        uint32_t flags = c.flags;
+        const uint32_t n = total;
+        if (any_stop) flags |= kFTimeout;
+        if (hopeless || over) flags |= kFOverflow;
+        if (a.mode == kModeShardTopK) flags &= ~kFInf;
+        Q38S_TT(u, 4);
+        Q38S_TR(u, 5, (static_cast<unsigned long long>(flags) << 32) | n);
+        uint32_t keep = 0;
+        if (!(flags & (kFTimeout | kFInf | kFOverflow))) {
+            keep = finish_buffer(cand, n, r, sorted, c);
+            if (keep == 0xffffffffu) flags |= kFOverflow;
+        }
+        Q38S_TT(u, 7);
+        Q38S_TR(u, 11, keep);
+        Q38S_TR(u, 12, blockIdx.x);
+        if (S == 1) {
+            Q38S_TR(u, 8, (flags & kFOverflow) ? 1 : (flags ? 2 : 0));
+            finish_row<DT>(a, r, flags, sorted, keep, area, c);
+            Q38S_TT(u, 9);
+            cbar();
+            continue;
+        }
+        // ---- multi-segment row: park the list, the last segment merges
+        {
+            const size_t base = static_cast<size_t>(u) * kSegCap;
+            const uint32_t len = (flags & (kFTimeout | kFInf | kFOverflow)) ? 0u : keep;
+            for (uint32_t i = tid; i < len; i += kCons) a.seg_keys[base + i] = sorted[i];
+            if (tid == 0) {
+                a.seg_hdr[u * 4 + 0] = len;
+                a.seg_hdr[u * 4 + 1] = flags;
+            }
+            __threadfence();
+            cbar();
+            if (tid == 0) c.bc_u32[2] = atomicAdd(&a.row_ticket[v], 1u) == S - 1;
+            cbar();
+            if (!c.bc_u32[2]) {
+                Q38S_TR(u, 8, 3);
+                Q38S_TT(u, 9);
+                continue;
+            }
+            __threadfence();
+            // segment headers in parallel (thread s reads segment s), then
+            // every segment's list lands at its prefix offset in cand
+            uint32_t my_len = 0, my_flags = 0;
+            if (tid < S) {
+                my_len = __ldcg(&a.seg_hdr[(v * S + tid) * 4 + 0]);
+                my_flags = __ldcg(&a.seg_hdr[(v * S + tid) * 4 + 1]);
+            }
+            uint32_t rtotal;
+            const uint32_t rel_off = cscan_excl(my_len, &rtotal, c);
+            uint32_t rflags = cor_u32(my_flags, c);
+            if (a.mode == kModeShardTopK) rflags &= ~kFInf;
+            uint32_t rkeep = 0;
+            if (!(rflags & (kFTimeout | kFInf | kFOverflow)) && rtotal > kBuf) rflags |= kFOverflow;
+            if (!(rflags & (kFTimeout | kFInf | kFOverflow))) {
+                cbar();
+                if (tid < S) {
+                    c.hist[tid] = my_len;
+                    c.hist[128 + tid] = rel_off;
+                }
+                cbar();
+                // warp w copies segments w, w + 8, ... with lane-strided loads
+                for (uint32_t s2 = warp; s2 < S; s2 += kCons / 32) {
+                    const uint32_t len2 = c.hist[s2];
+                    const uint32_t off2 = c.hist[128 + s2];
+                    const uint64_t* src = a.seg_keys + static_cast<size_t>(v * S + s2) * kSegCap;
+                    for (uint32_t i = lane; i < len2; i += 32)
+                        cand[off2 + i] = __ldcg(reinterpret_cast<const unsigned long long*>(src + i));
+                }
+                cbar();
+                rkeep = finish_buffer(cand, rtotal, r, sorted, c);
+                if (rkeep == 0xffffffffu) rflags |= kFOverflow;
+            }
+            if (tid == 0) a.row_ticket[v] = 0;  // every segment has arrived: reset for the next call
+            Q38S_TR(u, 8, 4 + ((rflags & kFOverflow) ? 1 : 0));
+            finish_row<DT>(a, r, rflags, sorted, rkeep, area, c);
+            Q38S_TT(u, 9);
+            cbar();
+        }
+    }
+    const bool aborted = *reinterpret_cast<volatile uint32_t*>(&c.abort_flag) != 0;
+    cbar();
+    if (aborted || stop) {
+        // let the producer stop, then let copies still in flight land before
+        // the CTA's shared memory goes away
+        if (tid == 0) {
+            atomicOr(&c.abort_flag, 1u);
+            const long long start = clock64();
+            while (!*reinterpret_cast<volatile uint32_t*>(&c.prod_done) &&
+                   clock64() - start < kWaitLimitCycles) {
+            }
+            const uint32_t issued = *reinterpret_cast<volatile uint32_t*>(&c.issued);
+            const uint32_t from = min(c.fail_g, g);
+            for (uint32_t x = from; x < issued; ++x)
+                mbar_wait_bounded(&c.full[x % kRing], (x / kRing) & 1u, kWaitLimitCycles);
+        }
+        cbar();
+    }
+}
+
+}  // namespace
+
+size_t stream_smem_bytes() { return kRing * kSlot + kArea; }
+
+#ifdef Q38S_TRACE
+}  // namespace q38s
+extern "C" int q38s_trace_install(unsigned long long* buf) {
+    return static_cast<int>(cudaMemcpyToSymbol(q38s::g_trace, &buf, sizeof(buf)));
+}
+namespace q38s {
+#endif
+
+uint32_t stream_segments(uint32_t vrows, uint32_t vocab, int device) {
+    static int sms_cache[64] = {};
+    int sms = device >= 0 && device < 64 ? sms_cache[device] : 0;
+    if (sms == 0) {
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        if (sms <= 0) sms = 148;
+        if (device >= 0 && device < 64) sms_cache[device] = sms;
+    }
+    const uint32_t slots = 2u * static_cast<uint32_t>(sms);
+    if (vrows == 0 || vrows * 2 >= slots) return 1;
+    uint32_t s = slots / vrows;
+    const uint32_t nblk = (vocab + 127) / 128;
+    const uint32_t by_cols = nblk / 16;  // segments of at least 2,048 columns
+    if (s > by_cols) s = by_cols;
+    if (s > 64) s = 64;
+    while (s > 1 && vrows * s > kMaxSegUnits) --s;
+    return s < 1 ? 1 : s;
+}
+
+template <int DT>
+static int launch_stream_t(const SampleArgs& a, void* stream) {
+    auto kern = stream_kernel<DT>;
+    const size_t smem = stream_smem_bytes();
+    static bool configured[2][64] = {};
+    static int sms[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const int slot = DT == Q38S_DTYPE_BF16 ? 0 : 1;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[slot][dev]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        configured[slot][dev] = true;
+    }
+    const uint32_t units = a.vrows * a.segs;
+    const uint32_t cap = 2u * static_cast<uint32_t>(sms[dev]);
+    const uint32_t grid = units < cap ? units : cap;
+    kern<<<grid, kBlock, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    return cudaGetLastError();
+}
+
+int launch_stream(const SampleArgs& a, void* stream) {
+    if (a.vrows == 0) return cudaSuccess;
+    return a.dtype == Q38S_DTYPE_BF16 ? launch_stream_t<Q38S_DTYPE_BF16>(a, stream)
+                                      : launch_stream_t<Q38S_DTYPE_F32>(a, stream);
+}
+
+}  // namespace q38s
