@@ -223,7 +223,7 @@ int create_batch(int device, uint32_t full_vocab, uint32_t col_begin, uint32_t c
         alloc(reinterpret_cast<void**>(&b->d_counts),
               sizeof(uint32_t) * static_cast<size_t>(columns) * rows);
     alloc(reinterpret_cast<void**>(&b->d_scratch),
-          sizeof(uint32_t) * static_cast<size_t>(columns) * rows);
+          2 * sizeof(uint32_t) * static_cast<size_t>(columns) * rows);  // keys, weights
     b->scratch_rows = rows;
     const size_t tickets = std::max<size_t>(rows, kMtpRows);
     alloc(reinterpret_cast<void**>(&b->d_seg_keys),
@@ -285,6 +285,7 @@ SampleArgs base_args(const q38s_batch* b, const void* logits, uint16_t dtype,
     a.counts = b->d_counts;
     a.vrow_state_const = ~0u;
     a.scratch = b->d_scratch;
+    a.scratch_w = reinterpret_cast<float*>(b->d_scratch + static_cast<size_t>(b->vocab) * b->rows);
     a.seg_keys = b->d_seg_keys;
     a.seg_hdr = b->d_seg_hdr;
     a.row_ticket = b->d_row_ticket;
@@ -432,8 +433,8 @@ int q38s_mtp_verify(const q38s_batch* bc, uint32_t row, const void* target, cons
                     "speculative verification needs 0 < top_k <= 1024");
     DeviceGuard g(b->device);
     if (!b->d_mtp_scratch) {
-        cudaError_t e = cudaMalloc(&b->d_mtp_scratch,
-                                   sizeof(uint32_t) * static_cast<size_t>(b->vocab) * kMtpRows);
+        cudaError_t e = cudaMalloc(&b->d_mtp_scratch,  // keys, weights
+                                   2 * sizeof(uint32_t) * static_cast<size_t>(b->vocab) * kMtpRows);
         if (e == cudaSuccess)
             e = cudaMalloc(&b->d_mtp_tokens, sizeof(int32_t) * kLeaderCap * kMtpRows);
         if (e == cudaSuccess)
@@ -461,6 +462,7 @@ int q38s_mtp_verify(const q38s_batch* bc, uint32_t row, const void* target, cons
     a.dist.n_retained = b->d_mtp_nret;
     a.dist.n_candidates = b->d_mtp_ncand;
     a.scratch = b->d_mtp_scratch;
+    a.scratch_w = reinterpret_cast<float*>(b->d_mtp_scratch + static_cast<size_t>(b->vocab) * kMtpRows);
     a.mtp = result;
     a.n_draft = n_draft;
     a.draft_tokens = draft_tokens;

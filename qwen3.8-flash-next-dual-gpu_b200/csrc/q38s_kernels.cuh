@@ -72,8 +72,10 @@ struct SampleArgs {
     q38s_distribution dist;
     q38s_candidate* topk_out;  // kModeShardTopK: vrows * k_out entries
     uint32_t k_out;
-    // general-path scratch: one vocab-sized key array per virtual row
+    // general-path scratch: one vocab-sized key array per virtual row, and
+    // one vocab-sized float weight array per virtual row
     uint32_t* scratch;
+    float* scratch_w;
     // speculative verification, run by the last row to finish
     q38s_mtp_result* mtp;
     uint32_t n_draft;

@@ -57,6 +57,7 @@ constexpr uint32_t kBuf = 2048;                  // candidate buffer (rank keys)
 constexpr uint32_t kSlice = kBuf / (kCons / 32);  // candidate slice of one consumer warp
 constexpr uint32_t kShrinkAt = kSlice - 32;      // warp compaction trigger
 constexpr int kWarpPer = kSlice / 32;            // slice entries per lane
+constexpr uint32_t kStage = 64;                  // staged exact evaluations per warp round
 constexpr uint32_t kFinal = kSegCap;             // candidates entering the epilogue
 constexpr uint32_t kGather = 1024;               // exact gather of the general path
 constexpr uint32_t kArea = 32768;                // candidate / epilogue work area
@@ -103,6 +104,7 @@ struct __align__(16) Ctl {
     uint32_t mrun;         // running maximum of exact candidate keys
     uint32_t fail_g;       // first tile a consumer warp gave up waiting for
     uint32_t wcnt[kCons / 32];  // per-warp slice lengths at the end of a unit
+    uint32_t stage[kCons / 32][kStage];  // per-warp tile indices awaiting exact values
     uint32_t bc_u32[4];
     uint64_t bc_u64[2];
     uint32_t red_u32[kCons / 32];
@@ -212,6 +214,7 @@ struct Row {
     uint32_t v;           // virtual row
     uint32_t srow;        // state row
     RowParams p;
+    RowState st;          // the state row as of the launch
     uint64_t rng_before;
     uint32_t k_eff;       // 0: no top-k truncation
     bool pen, nonmono, freq, minp;
@@ -231,8 +234,8 @@ __device__ void load_row(const SampleArgs& a, uint32_t v, Row& r) {
     r.srow = state_row(a, v);
     r.p = a.params[r.srow];
     const uint32_t off = v < a.split ? v : v - a.split;
-    r.rng_before = a.state[r.srow].rng_state +
-                   (a.rng_step ? static_cast<uint64_t>(off) * kGamma : 0ull);
+    r.st = a.state[r.srow];
+    r.rng_before = r.st.rng_state + (a.rng_step ? static_cast<uint64_t>(off) * kGamma : 0ull);
     r.pen = (r.p.flags & kFlagPenalties) != 0;
     r.nonmono = (r.p.flags & kFlagNonMonotone) != 0;
     r.freq = (r.p.flags & kFlagFrequency) != 0;
@@ -373,25 +376,6 @@ __device__ __forceinline__ void hist_inc(uint32_t* hist, uint32_t bin, bool acti
         const uint32_t peers = __match_any_sync(act, bin);
         if ((threadIdx.x & 31) == static_cast<uint32_t>(__ffs(peers) - 1))
             atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
-    }
-}
-// Same with a 64-bit mass per lane: one round per distinct bin in the warp.
-__device__ __forceinline__ void hist_inc_mass(uint32_t* hist, uint64_t* hmass, uint32_t bin,
-                                              uint64_t mass, bool active) {
-    uint32_t todo = __ballot_sync(0xffffffffu, active);
-    while (todo) {
-        const uint32_t leader = __ffs(todo) - 1;
-        const uint32_t lb = __shfl_sync(0xffffffffu, bin, leader);
-        const bool mine = active && bin == lb;
-        const uint32_t m = __ballot_sync(0xffffffffu, mine);
-        uint64_t sum = mine ? mass : 0ull;
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if ((threadIdx.x & 31) == leader) {
-            atomicAdd(&hist[lb], static_cast<uint32_t>(__popc(m)));
-            atomicAdd(reinterpret_cast<unsigned long long*>(&hmass[lb]),
-                      static_cast<unsigned long long>(sum));
-        }
-        todo &= ~m;
     }
 }
 // Appends `key` for every lane with `push` set; one atomic per warp.  The
@@ -746,7 +730,9 @@ __device__ void write_decision(const SampleArgs& a, const Row& r, int32_t token,
     if (a.decisions) a.decisions[r.v] = d;
     if (a.mode == kModeSampleCommit && status == Q38S_ROW_OK) {
         // commit (sampling.cc:148-156) then commit_token (sampling.cc:163-172)
-        RowState& s = a.state[r.srow];
+        // (the state was read at the start of the row; only this row's
+        // commit changes it, so it is written without a read)
+        RowState s = r.st;
         s.rng_state = d.rng_after;
         s.sampled_tokens += 1;
         const uint32_t col = static_cast<uint32_t>(token) - a.col_begin;
@@ -756,6 +742,7 @@ __device__ void write_decision(const SampleArgs& a, const Row& r, int32_t token,
         s.canonical_tokens += 1;
         s.penalty_checksum ^= splitmix64(static_cast<uint64_t>(static_cast<uint32_t>(token)) ^
                                          (s.canonical_tokens * kGamma));
+        a.state[r.srow] = s;
     }
 }
 
@@ -934,9 +921,42 @@ __device__ __forceinline__ bool in_k0(const Cut& g, uint32_t key, uint32_t tok) 
     if (!g.has_cut) return true;
     return key > g.cut_key || (key == g.cut_key && tok <= g.cut_tok);
 }
-__device__ __forceinline__ uint64_t wfix(const Cut& g, uint32_t key) {
-    const double w = exp(static_cast<double>(__fsub_rn(key_float(key), g.M)));
-    return static_cast<uint64_t>(w * kFix + 0.5);
+// Weight of a key relative to the row maximum M, as the mass-weighted
+// selection stores it: exp((double)(v - M)) rounded to float (the fixed-point
+// masses built from it are within 2^-24 relative of the double weights).
+__device__ __forceinline__ float weight_of(uint32_t key, float M) {
+    return static_cast<float>(exp(static_cast<double>(__fsub_rn(key_float(key), M))));
+}
+__device__ __forceinline__ uint64_t wfix(float w) {
+    return static_cast<uint64_t>(static_cast<double>(w) * kFix + 0.5);
+}
+
+// Visits every column j < V of the row's scratch arrays, eight per thread
+// per round with the loads issued first (memory-level parallelism for
+// L2-resident arrays); f(j, key, weight, valid) runs a warp-uniform number
+// of rounds (valid is false past the end), so f may use warp collectives.
+// `wts` may be null (weight 0).
+template <typename F>
+__device__ __forceinline__ void for_keys(const uint32_t* keys, const float* wts, uint32_t V,
+                                         F&& f) {
+    constexpr uint32_t kStep = 8 * kCons;
+    const uint32_t rounds = (V + kStep - 1) / kStep;
+    for (uint32_t b = 0; b < rounds; ++b) {
+        const uint32_t j0 = b * kStep + threadIdx.x;
+        uint32_t kk[8];
+        float ww[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t j = j0 + i * kCons;
+            kk[i] = j < V ? keys[j] : 0u;
+            ww[i] = (wts && j < V) ? wts[j] : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t j = j0 + i * kCons;
+            f(j, kk[i], ww[i], j < V);
+        }
+    }
 }
 
 struct Sel {
@@ -949,10 +969,11 @@ struct Sel {
 // Radix selection over the row's exact keys (global scratch, one per
 // column) restricted to K0 (or to key >= minp_key when !restrict_k0): the
 // first element in canonical order (value desc, token asc) at which the
-// running count (weighted = false) or fixed-point mass (weighted = true)
+// running count (wts == null) or fixed-point mass (wts: the stored weights)
 // reaches tau (>= tau, or > tau when strict).
-__device__ Sel row_select(const uint32_t* keys, uint32_t V, uint32_t tok0, const Cut& g0,
-                          bool restrict_k0, bool weighted, uint64_t tau, bool strict, Ctl& c) {
+__device__ Sel row_select(const uint32_t* keys, const float* wts, uint32_t V, uint32_t tok0,
+                          const Cut& g0, bool restrict_k0, uint64_t tau, bool strict, Ctl& c) {
+    const bool weighted = wts != nullptr;
     Cut g = g0;
     if (!restrict_k0) g.has_cut = false;
     uint32_t prefix = 0, mask = 0;
@@ -965,14 +986,14 @@ __device__ Sel row_select(const uint32_t* keys, uint32_t V, uint32_t tok0, const
         c.hist[threadIdx.x] = 0;
         c.hmass[threadIdx.x] = 0;
         cbar();
-        const uint32_t Vr = (V + kCons - 1) / kCons * kCons;
-        for (uint32_t j = threadIdx.x; j < Vr; j += kCons) {
-            const uint32_t key = j < V ? keys[j] : 0u;
-            const bool act = j < V && (key & mask) == prefix && in_k0(g, key, tok0 + j);
+        for_keys(keys, wts, V, [&](uint32_t j, uint32_t key, float w, bool valid) {
+            const bool act = valid && (key & mask) == prefix && in_k0(g, key, tok0 + j);
             const uint32_t d = (key >> shift) & 255u;
-            if (weighted) hist_inc_mass(c.hist, c.hmass, d, act ? wfix(g, key) : 0ull, act);
-            else hist_inc(c.hist, d, act);
-        }
+            hist_inc(c.hist, d, act);
+            if (weighted && act)
+                atomicAdd(reinterpret_cast<unsigned long long*>(&c.hmass[d]),
+                          static_cast<unsigned long long>(wfix(w)));
+        });
         cbar();
         if (threadIdx.x == 0) {
             uint64_t acc = above;
@@ -1002,7 +1023,7 @@ __device__ Sel row_select(const uint32_t* keys, uint32_t V, uint32_t tok0, const
     const uint32_t key = prefix;
     uint64_t j, per = 1;
     if (weighted) {
-        per = wfix(g, key);
+        per = wfix(weight_of(key, g.M));
         if (per == 0) {
             j = 0;
         } else if (strict) {
@@ -1015,34 +1036,44 @@ __device__ Sel row_select(const uint32_t* keys, uint32_t V, uint32_t tok0, const
         j = tau > above ? tau - above - 1 : 0;
     }
     if (j >= group) j = group - 1;
-    // the j-th smallest token of the group: radix over the token bits
-    uint32_t tprefix = 0, tmask = 0, need = static_cast<uint32_t>(j);
-    for (int level = 0; level < 4; ++level) {
-        const int shift = 24 - 8 * level;
+    // the j-th smallest token of the group: a single member is found in one
+    // pass, larger groups by a radix over the token bits
+    uint32_t tprefix = 0;
+    if (group == 1) {
         cbar();
-        c.hist[threadIdx.x] = 0;
+        for_keys(keys, nullptr, V, [&](uint32_t x, uint32_t k2, float, bool valid) {
+            if (valid && k2 == key && in_k0(g, key, tok0 + x)) c.bc_u32[3] = tok0 + x;
+        });
         cbar();
-        const uint32_t Vr = (V + kCons - 1) / kCons * kCons;
-        for (uint32_t x = threadIdx.x; x < Vr; x += kCons) {
-            const uint32_t tok = tok0 + x;
-            const bool act =
-                x < V && keys[x] == key && (tok & tmask) == tprefix && in_k0(g, key, tok);
-            hist_inc(c.hist, (tok >> shift) & 255u, act);
-        }
-        cbar();
-        if (threadIdx.x == 0) {
-            uint32_t left = need, d = 0;
-            for (; d < 255; ++d) {
-                if (left < c.hist[d]) break;
-                left -= c.hist[d];
+        tprefix = c.bc_u32[3];
+    } else {
+        uint32_t tmask = 0, need = static_cast<uint32_t>(j);
+        for (int level = 0; level < 4; ++level) {
+            const int shift = 24 - 8 * level;
+            cbar();
+            c.hist[threadIdx.x] = 0;
+            cbar();
+            for_keys(keys, nullptr, V, [&](uint32_t x, uint32_t k2, float, bool valid) {
+                const uint32_t tok = tok0 + x;
+                const bool act =
+                    valid && k2 == key && (tok & tmask) == tprefix && in_k0(g, key, tok);
+                hist_inc(c.hist, (tok >> shift) & 255u, act);
+            });
+            cbar();
+            if (threadIdx.x == 0) {
+                uint32_t left = need, d = 0;
+                for (; d < 255; ++d) {
+                    if (left < c.hist[d]) break;
+                    left -= c.hist[d];
+                }
+                c.bc_u32[0] = d;
+                c.bc_u32[1] = left;
             }
-            c.bc_u32[0] = d;
-            c.bc_u32[1] = left;
+            cbar();
+            tprefix |= c.bc_u32[0] << shift;
+            tmask |= 255u << shift;
+            need = c.bc_u32[1];
         }
-        cbar();
-        tprefix |= c.bc_u32[0] << shift;
-        tmask |= 255u << shift;
-        need = c.bc_u32[1];
     }
     res.found = true;
     res.key = key;
@@ -1056,6 +1087,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
     const uint32_t V = a.vocab;
     const uint32_t tok0 = a.col_begin;
     uint32_t* keys = a.scratch + static_cast<size_t>(r.v) * V;
+    float* wts = a.scratch_w + static_cast<size_t>(r.v) * V;
     const unsigned char* row = row_ptr<DT>(a, r.v);
     // this call's penalised columns in shared memory when they fit
     const uint32_t words = (V + 31) / 32;
@@ -1072,26 +1104,37 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         cbar();
         pbm = sbm;
     }
-    // G0: exact key of every column
+    // G0: exact key of every column (eight loads in flight per thread)
     uint32_t kmax = 0;
-    for (uint32_t j = threadIdx.x; j < V; j += kCons) {
-        const float x = load_elem<DT>(row, j);
-        bool penalized = false;
-        uint64_t count = 1;
-        if (r.pen) {
-            if (pbm) {
-                penalized = (pbm[j >> 5] >> (j & 31)) & 1u;
-                if (penalized && r.freq)
-                    count = (r.counts_row ? r.counts_row[j] : 0u) + extra_count(r, tok0 + j);
-            } else {
-                const uint64_t ex = extra_count(r, tok0 + j);
-                penalized = ((r.gbm[j >> 5] >> (j & 31)) & 1u) || ex;
-                if (penalized && r.freq) count = (r.counts_row ? r.counts_row[j] : 0u) + ex;
-            }
+    constexpr uint32_t kStep = 8 * kCons;
+    for (uint32_t b = 0; b < (V + kStep - 1) / kStep; ++b) {
+        float xs[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t j = b * kStep + threadIdx.x + i * kCons;
+            xs[i] = j < V ? load_elem<DT>(row, j) : 0.0f;
         }
-        const uint32_t k = float_key(transform(x, penalized, count, r.p));
-        keys[j] = k;
-        kmax = max(kmax, k);
+#pragma unroll 1
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t j = b * kStep + threadIdx.x + i * kCons;
+            if (j >= V) break;
+            bool penalized = false;
+            uint64_t count = 1;
+            if (r.pen) {
+                if (pbm) {
+                    penalized = (pbm[j >> 5] >> (j & 31)) & 1u;
+                    if (penalized && r.freq)
+                        count = (r.counts_row ? r.counts_row[j] : 0u) + extra_count(r, tok0 + j);
+                } else {
+                    const uint64_t ex = extra_count(r, tok0 + j);
+                    penalized = ((r.gbm[j >> 5] >> (j & 31)) & 1u) || ex;
+                    if (penalized && r.freq) count = (r.counts_row ? r.counts_row[j] : 0u) + ex;
+                }
+            }
+            const uint32_t k = float_key(exact_value(xs[i], penalized, count, r.p));
+            keys[j] = k;
+            kmax = max(kmax, k);
+        }
     }
     Cut g;
     g.M_key = cmax_u32(kmax, c);  // its barriers also publish keys[] to the CTA
@@ -1122,11 +1165,13 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
     }
     // G2: the kept set K0 = top-k of {key >= minp_key}
     uint32_t cnt = 0;
-    for (uint32_t j = threadIdx.x; j < V; j += kCons) cnt += keys[j] >= g.minp_key;
+    for_keys(keys, nullptr, V, [&](uint32_t, uint32_t key, float, bool valid) {
+        cnt += valid && key >= g.minp_key;
+    });
     const uint32_t c_minp = csum_u32(cnt, c);
     const uint32_t n0 = r.k_eff ? min(r.k_eff, c_minp) : c_minp;
     if (n0 < c_minp) {
-        const Sel cut = row_select(keys, V, tok0, g, false, false, n0, false, c);
+        const Sel cut = row_select(keys, nullptr, V, tok0, g, false, n0, false, c);
         g.has_cut = true;
         g.cut_key = cut.key;
         g.cut_tok = cut.token;
@@ -1138,12 +1183,10 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         cbar();
         if (threadIdx.x == 0) c.bc_u32[2] = 0;
         cbar();
-        const uint32_t Vr = (V + kCons - 1) / kCons * kCons;
-        for (uint32_t j = threadIdx.x; j < Vr; j += kCons) {
-            const uint32_t k = j < V ? keys[j] : 0u;
-            const bool act = j < V && in_k0(g, k, tok0 + j);
+        for_keys(keys, nullptr, V, [&](uint32_t j, uint32_t k, float, bool valid) {
+            const bool act = valid && in_k0(g, k, tok0 + j);
             warp_push(act, rank_key(k, tok0 + j), gk, kGather, &c.bc_u32[2]);
-        }
+        });
         cbar();
         const uint32_t m = min(c.bc_u32[2], kGather);
         sort_desc(gk, m, lk);
@@ -1153,14 +1196,17 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         row_output(a, r, lk, m, w, S, q, c);
         return;
     }
-    // G4: large kept set: fixed-point masses (2^-43 units) locate the top-p
-    // cut and the draw
+    // G4: large kept set: weights once (float), then fixed-point masses
+    // (2^-43 units) locate the top-p cut and the draw
     uint64_t part = 0;
-    for (uint32_t j = threadIdx.x; j < V; j += kCons) {
-        const uint32_t k = keys[j];
-        if (in_k0(g, k, tok0 + j)) part += wfix(g, k);
-    }
-    const uint64_t Z = csum_u64(part, c);
+    for_keys(keys, nullptr, V, [&](uint32_t j, uint32_t k, float, bool valid) {
+        if (!valid) return;
+        const bool in = in_k0(g, k, tok0 + j);
+        const float w = in ? weight_of(k, g.M) : 0.0f;
+        wts[j] = w;
+        part += wfix(w);
+    });
+    const uint64_t Z = csum_u64(part, c);  // its barriers also publish wts[]
     int32_t status = Q38S_ROW_OK;
     int32_t token = -1;
     uint64_t Zr = Z;
@@ -1169,7 +1215,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
     if (status == Q38S_ROW_OK && r.p.top_p < 1.0f) {
         const uint64_t tau = static_cast<uint64_t>(static_cast<double>(r.p.top_p) *
                                                    static_cast<double>(Z));
-        cutp = row_select(keys, V, tok0, g, true, true, tau, false, c);
+        cutp = row_select(keys, wts, V, tok0, g, true, tau, false, c);
         if (cutp.found) Zr = cutp.through;
     }
     double draw_d = 0.0;
@@ -1177,7 +1223,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         const double u = uniform01(r.rng_before + kGamma);
         const uint64_t draw = static_cast<uint64_t>(u * static_cast<double>(Zr));
         draw_d = static_cast<double>(draw) / kFix;
-        const Sel sel = row_select(keys, V, tok0, g, true, true, draw, true, c);
+        const Sel sel = row_select(keys, wts, V, tok0, g, true, draw, true, c);
         if (sel.found) token = static_cast<int32_t>(sel.token);
         else if (cutp.found) token = static_cast<int32_t>(cutp.token);
         else status = Q38S_ROW_NORMALIZATION;
@@ -1460,18 +1506,19 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                     for (int q = 0; q < kU; ++q) m = fmaxf(m, vec_max<DT>(wv[q]));
                     hit = !(m < rho);
                 }
-                // rare path: exact values of the hits into the warp's slice;
-                // rolled loops keep it small
+                // rare path: the warp gathers every element of its part of the
+                // tile that may reach theta (raw value at or above theta's raw
+                // bound, or penalised in a row whose penalties can raise a
+                // value), stages their tile indices, evaluates them exactly
+                // one per lane, and appends those at or above theta to its
+                // slice.  Rolled loops keep the code small.
                 if (__any_sync(kFull, hit || r.nonmono)) {
                     const uint32_t tokt = a.col_begin + t0;
-                    uint32_t wmax = 0;
-                    bool inf = false;
-#pragma unroll 1
+                    uint32_t look = 0;  // bit q * pv + e: element e of vector q
+#pragma unroll
                     for (int q = 0; q < kU; ++q) {
                         const uint32_t j = tid + q * kCons;
-                        uint32_t look = 0;
                         if (j < nvec) {
-                            const uint4 w4 = vec[j];
                             uint32_t penbits = 0;
                             if (r.nonmono) {
                                 const uint32_t e0 = j * pv;
@@ -1479,17 +1526,43 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                             }
 #pragma unroll
                             for (int e = 0; e < static_cast<int>(pv); ++e) {
-                                const float x = vec_elem<DT>(w4, e);
+                                const float x = vec_elem<DT>(wv[q], e);
                                 if ((!(x < rho) || ((penbits >> e) & 1u)) && j * pv + e < n)
-                                    look |= 1u << e;
+                                    look |= 1u << (q * pv + e);
                             }
                         }
-                        while (__any_sync(kFull, look != 0)) {
+                    }
+                    // lane offsets of the looks (inclusive warp prefix sum)
+                    const uint32_t mine = __popc(look);
+                    uint32_t incl = mine;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const uint32_t y = __shfl_up_sync(kFull, incl, o);
+                        if (lane >= static_cast<uint32_t>(o)) incl += y;
+                    }
+                    const uint32_t all = __shfl_sync(kFull, incl, 31);
+                    uint32_t* stg = c.stage[warp];
+                    uint32_t wmax = 0;
+                    bool inf = false;
+#pragma unroll 1
+                    for (uint32_t base = 0; base < all; base += kStage) {
+                        uint32_t lk = look, pos = incl - mine;
+                        while (lk) {
+                            const uint32_t b = __ffs(lk) - 1;
+                            lk &= lk - 1;
+                            if (pos >= base && pos < base + kStage)
+                                stg[pos - base] = (tid + (b / pv) * kCons) * pv + (b % pv);
+                            ++pos;
+                        }
+                        __syncwarp();
+                        const uint32_t m = min(kStage, all - base);
+#pragma unroll 1
+                        for (uint32_t i0 = 0; i0 < m; i0 += 32) {
+                            const uint32_t i = i0 + lane;
                             uint32_t k = 0, idx = 0;
                             bool push = false;
-                            if (look) {
-                                idx = j * pv + (__ffs(look) - 1);
-                                look &= look - 1;
+                            if (i < m) {
+                                idx = stg[i];
                                 const float vx = eval_slot(r, sbm, load_elem<DT>(sl, idx), idx,
                                                            t0 + idx, tokt + idx);
                                 inf |= vx == INFINITY;
@@ -1499,8 +1572,8 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                             }
                             const uint32_t pm = __ballot_sync(kFull, push);
                             if (push) {
-                                const uint32_t pos = cnt + __popc(pm & ((1u << lane) - 1u));
-                                if (pos < kSlice) slice[pos] = rank_key(k, tokt + idx);
+                                const uint32_t pos2 = cnt + __popc(pm & ((1u << lane) - 1u));
+                                if (pos2 < kSlice) slice[pos2] = rank_key(k, tokt + idx);
                             }
                             cnt += __popc(pm);
                             if (cnt > kSlice) wover = true;
@@ -1512,6 +1585,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                                 if (cnt > kShrinkAt) wover = true;
                             }
                         }
+                        __syncwarp();
                     }
                     wmax = __reduce_max_sync(kFull, wmax);
                     if (__any_sync(kFull, inf) && lane == 0) atomicOr(&c.flags, kFInf);
