@@ -378,6 +378,24 @@ __device__ __forceinline__ void hist_inc(uint32_t* hist, uint32_t bin, bool acti
             atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
     }
 }
+// Same with a fixed-point mass per lane (below 2^44): the lanes of a bin
+// add their masses exactly as two 22-bit limbs with warp reductions, and one
+// lane per bin updates the shared counters.  The whole warp calls it.
+__device__ __forceinline__ void hist_inc_mass(uint32_t* hist, uint64_t* hmass, uint32_t bin,
+                                              uint64_t mass, bool active) {
+    const uint32_t act = __ballot_sync(0xffffffffu, active);
+    if (active) {
+        const uint32_t peers = __match_any_sync(act, bin);
+        const uint32_t lo = __reduce_add_sync(peers, static_cast<uint32_t>(mass & 0x3fffffu));
+        const uint32_t hi = __reduce_add_sync(peers, static_cast<uint32_t>(mass >> 22));
+        if ((threadIdx.x & 31) == static_cast<uint32_t>(__ffs(peers) - 1)) {
+            atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
+            atomicAdd(reinterpret_cast<unsigned long long*>(&hmass[bin]),
+                      static_cast<unsigned long long>(lo) +
+                          (static_cast<unsigned long long>(hi) << 22));
+        }
+    }
+}
 // Appends `key` for every lane with `push` set; one atomic per warp.  The
 // whole warp calls it.  Returns true when the buffer overflowed.
 __device__ __forceinline__ bool warp_push(bool push, uint64_t key, uint64_t* buf, uint32_t cap,
@@ -922,10 +940,11 @@ __device__ __forceinline__ bool in_k0(const Cut& g, uint32_t key, uint32_t tok) 
     return key > g.cut_key || (key == g.cut_key && tok <= g.cut_tok);
 }
 // Weight of a key relative to the row maximum M, as the mass-weighted
-// selection stores it: exp((double)(v - M)) rounded to float (the fixed-point
-// masses built from it are within 2^-24 relative of the double weights).
+// selection stores it: expf(v - M) in single precision (within a few 2^-24
+// relative of the reference's double weights; this path is approximate by
+// construction and its draws count as boundary cases).
 __device__ __forceinline__ float weight_of(uint32_t key, float M) {
-    return static_cast<float>(exp(static_cast<double>(__fsub_rn(key_float(key), M))));
+    return expf(__fsub_rn(key_float(key), M));
 }
 __device__ __forceinline__ uint64_t wfix(float w) {
     return static_cast<uint64_t>(static_cast<double>(w) * kFix + 0.5);
@@ -989,10 +1008,8 @@ __device__ Sel row_select(const uint32_t* keys, const float* wts, uint32_t V, ui
         for_keys(keys, wts, V, [&](uint32_t j, uint32_t key, float w, bool valid) {
             const bool act = valid && (key & mask) == prefix && in_k0(g, key, tok0 + j);
             const uint32_t d = (key >> shift) & 255u;
-            hist_inc(c.hist, d, act);
-            if (weighted && act)
-                atomicAdd(reinterpret_cast<unsigned long long*>(&c.hmass[d]),
-                          static_cast<unsigned long long>(wfix(w)));
+            if (weighted) hist_inc_mass(c.hist, c.hmass, d, act ? wfix(w) : 0ull, act);
+            else hist_inc(c.hist, d, act);
         });
         cbar();
         if (threadIdx.x == 0) {
@@ -1114,7 +1131,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
             const uint32_t j = b * kStep + threadIdx.x + i * kCons;
             xs[i] = j < V ? load_elem<DT>(row, j) : 0.0f;
         }
-#pragma unroll 1
+#pragma unroll
         for (int i = 0; i < 8; ++i) {
             const uint32_t j = b * kStep + threadIdx.x + i * kCons;
             if (j >= V) break;
@@ -1136,6 +1153,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
             kmax = max(kmax, k);
         }
     }
+    Q38S_TT(r.v, 6);
     Cut g;
     g.M_key = cmax_u32(kmax, c);  // its barriers also publish keys[] to the CTA
     g.M = key_float(g.M_key);
@@ -1176,6 +1194,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         g.cut_key = cut.key;
         g.cut_tok = cut.token;
     }
+    Q38S_TT(r.v, 10);
     if (n0 <= kGather) {
         // G3: gather K0, sort, finish exactly
         uint64_t* gk = reinterpret_cast<uint64_t*>(area + kGather * 8);  // unsorted
@@ -1207,6 +1226,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         part += wfix(w);
     });
     const uint64_t Z = csum_u64(part, c);  // its barriers also publish wts[]
+    Q38S_TT(r.v, 13);
     int32_t status = Q38S_ROW_OK;
     int32_t token = -1;
     uint64_t Zr = Z;
@@ -1218,6 +1238,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         cutp = row_select(keys, wts, V, tok0, g, true, tau, false, c);
         if (cutp.found) Zr = cutp.through;
     }
+    Q38S_TT(r.v, 14);
     double draw_d = 0.0;
     if (status == Q38S_ROW_OK) {
         const double u = uniform01(r.rng_before + kGamma);
@@ -1228,6 +1249,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         else if (cutp.found) token = static_cast<int32_t>(cutp.token);
         else status = Q38S_ROW_NORMALIZATION;
     }
+    Q38S_TT(r.v, 15);
     write_decision(a, r, token, status);
     if (a.dist.capacity && threadIdx.x == 0) {
         if (a.dist.n_candidates) a.dist.n_candidates[r.v] = n0;
