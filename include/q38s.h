@@ -299,6 +299,39 @@ int q38s_shard_merge_sample(const q38s_batch* shard,
 int q38s_argmax_bf16(const uint16_t* logits, uint32_t count, int32_t* output,
                      void* stream, int device);
 
+/* ------------------------------------------------------------------------
+ * Sampling without device allocation.  No counterpart in the reference.
+ *
+ * For callers that must not allocate GPU memory themselves or through this
+ * library: code that runs inside a memory pool or arena it does not own, a
+ * plug-in loaded into a host process that forbids cudaMalloc after start-up,
+ * or a real-time loop in which an allocation (and the device-wide
+ * synchronisation it can cause) is not allowed.  Every working buffer lives
+ * in one fixed, statically sized device array inside this library (about
+ * 10.6 MB on every GPU that loads it, held until the process exits); the
+ * caller passes only inputs and outputs.
+ *
+ * prepare() (sampling.cc:59-146 plus min_p) for `rows` rows of device logits
+ * (row r at logits + r * row_stride elements, bf16 or f32) as freshly
+ * constructed samplers: no committed penalty history and no additional
+ * penalty tokens, so repetition / presence / frequency penalties have
+ * nothing to act on.  configs: host array of `rows` V2 configs (validated
+ * as q38s_batch_create does).  rng_states: host array of each row's
+ * SamplerStateV1::rng_state before the draw, or NULL for each config's
+ * seed.  decisions: device array of `rows` entries.  The result equals
+ * q38s_batch_prepare on a new batch with the same configs and states.
+ * Limits: 1 <= rows <= 4, vocabulary <= 262,144; larger sizes are rejected
+ * with Q38S_INVALID_ARGUMENT.  The first call on a device resolves and
+ * clears the static array (a synchronous step: make that first call before
+ * any stream capture).  Every call shares the array, so calls whose work
+ * overlaps on the GPU (other streams, other host threads) race; order them
+ * on one stream. */
+int q38s_prepare_noalloc(const void* logits, uint16_t dtype, uint32_t vocabulary,
+                         uint32_t rows, uint64_t row_stride,
+                         const q38s_sampling_config_v2* configs,
+                         const uint64_t* rng_states, q38s_decision_v1* decisions,
+                         void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

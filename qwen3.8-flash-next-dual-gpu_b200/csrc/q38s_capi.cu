@@ -799,3 +799,126 @@ int q38s_sampler_config(const q38s_sampler* s, q38s_sampling_config_v1* out) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------ no-allocation entry
+// q38s_prepare_noalloc: every working buffer of the sampling kernel lives in
+// one statically sized device array (one copy per GPU that loads the
+// library), so the call allocates nothing.  Host code only ever passes the
+// array's device address, resolved once per device with
+// cudaGetSymbolAddress; the array's name in host code is not an address.
+namespace {
+
+constexpr uint32_t kNoAllocRows = 4;
+constexpr uint32_t kNoAllocVocab = 262144;
+constexpr uint32_t kNoAllocBitmapWords = ((kNoAllocVocab + 127) / 128) * 4;
+
+struct NoAllocLayout {  // byte offsets into the static array
+    static constexpr size_t params = 0;
+    static constexpr size_t state = params + 256;
+    static constexpr size_t tickets = state + 256;
+    static constexpr size_t bitmap = tickets + 256;
+    static constexpr size_t seg_hdr =
+        bitmap + sizeof(uint32_t) * static_cast<size_t>(kNoAllocBitmapWords) * kNoAllocRows;  // zeros
+    static constexpr size_t seg_keys = seg_hdr + sizeof(uint32_t) * 4 * kMaxSegUnits;
+    static constexpr size_t keys =
+        seg_keys + sizeof(uint64_t) * static_cast<size_t>(kMaxSegUnits) * kSegCap;
+    static constexpr size_t weights =
+        keys + sizeof(uint32_t) * static_cast<size_t>(kNoAllocVocab) * kNoAllocRows;
+    static constexpr size_t end =
+        weights + sizeof(float) * static_cast<size_t>(kNoAllocVocab) * kNoAllocRows;
+};
+static_assert(sizeof(RowParams) * kNoAllocRows <= 256, "params slot");
+static_assert(sizeof(RowState) * kNoAllocRows <= 256, "state slot");
+static_assert(NoAllocLayout::end % 256 == 0, "layout");
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NoAllocLayout::end];
+
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[64] = {};  // device address per device ordinal
+
+// Once per device, with that device current: the array's device address,
+// and the zero penalty bitmap / tickets the kernel expects.
+int noalloc_setup(int device, unsigned char** out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (device < 0 || device >= 64) return fail(Q38S_CUDA_ERROR, "device ordinal out of range");
+    if (!g_noalloc_ptr[device]) {
+        void* p = nullptr;
+        Q38S_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "no-alloc scratch address");
+        Q38S_CUDA(cudaMemset(p, 0, NoAllocLayout::end), "no-alloc scratch clear");
+        g_noalloc_ptr[device] = static_cast<unsigned char*>(p);
+    }
+    *out = g_noalloc_ptr[device];
+    return Q38S_OK;
+}
+
+}  // namespace
+
+extern "C" int q38s_prepare_noalloc(const void* logits, uint16_t dtype, uint32_t vocabulary,
+                                    uint32_t rows, uint64_t row_stride,
+                                    const q38s_sampling_config_v2* configs,
+                                    const uint64_t* rng_states, q38s_decision_v1* decisions,
+                                    void* stream) {
+    if (!logits || !configs || !decisions) return fail(Q38S_INVALID_ARGUMENT, "null argument");
+    if (rows == 0 || rows > kNoAllocRows)
+        return fail(Q38S_INVALID_ARGUMENT,
+                    "q38s_prepare_noalloc takes 1 to 4 rows (its working memory is static)");
+    if (vocabulary == 0 || vocabulary > kNoAllocVocab)
+        return fail(Q38S_INVALID_ARGUMENT,
+                    "q38s_prepare_noalloc takes a vocabulary of at most 262,144 tokens");
+    if (dtype != Q38S_DTYPE_BF16 && dtype != Q38S_DTYPE_F32)
+        return fail(Q38S_INVALID_ARGUMENT, "logits dtype must be bf16 or f32");
+    if (row_stride < vocabulary) return fail(Q38S_INVALID_ARGUMENT, kMsgSize);
+    RowParams params[kNoAllocRows];
+    RowState states[kNoAllocRows];
+    for (uint32_t r = 0; r < rows; ++r) {
+        const int rc = validate_config(vocabulary, 2, configs[r]);
+        if (rc) return rc;
+        if (configs[r].mode == Q38S_MODE_GREEDY) return fail(Q38S_LOGIC_ERROR, kMsgGreedy);
+        params[r] = to_params(configs[r]);
+        states[r] = RowState{rng_states ? rng_states[r] : configs[r].seed, 0, 0, 0};
+    }
+    int device = 0;
+    Q38S_CUDA(cudaGetDevice(&device), "current device");
+    unsigned char* base = nullptr;
+    int rc = noalloc_setup(device, &base);
+    if (rc) return rc;
+    auto s = static_cast<cudaStream_t>(stream);
+    // per-call inputs into the array; the tickets start at zero
+    Q38S_CUDA(cudaMemcpyAsync(base + NoAllocLayout::params, params, sizeof(RowParams) * rows,
+                              cudaMemcpyHostToDevice, s),
+              "no-alloc parameters");
+    Q38S_CUDA(cudaMemcpyAsync(base + NoAllocLayout::state, states, sizeof(RowState) * rows,
+                              cudaMemcpyHostToDevice, s),
+              "no-alloc states");
+    Q38S_CUDA(cudaMemsetAsync(base + NoAllocLayout::tickets, 0, 256, s), "no-alloc tickets");
+    const uint32_t es = dtype == Q38S_DTYPE_BF16 ? 2u : 4u;
+    SampleArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.logits = logits;
+    a.logits2 = logits;
+    a.split = rows;
+    a.row_stride = row_stride;
+    a.dtype = dtype;
+    a.use_tma = (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && ((row_stride * es) % 16 == 0);
+    a.vocab = vocabulary;
+    a.full_vocab = vocabulary;
+    a.col_begin = 0;
+    a.vrows = rows;
+    a.mode = kModePrepare;
+    a.params = reinterpret_cast<const RowParams*>(base + NoAllocLayout::params);
+    a.state = reinterpret_cast<RowState*>(base + NoAllocLayout::state);
+    a.bitmap = reinterpret_cast<uint32_t*>(base + NoAllocLayout::bitmap);
+    a.bitmap_words = ((vocabulary + 127) / 128) * 4;
+    a.counts = nullptr;  // no history: every count is zero
+    a.vrow_state_const = ~0u;
+    a.decisions = decisions;
+    a.scratch = reinterpret_cast<uint32_t*>(base + NoAllocLayout::keys);
+    a.scratch_w = reinterpret_cast<float*>(base + NoAllocLayout::weights);
+    a.seg_keys = reinterpret_cast<uint64_t*>(base + NoAllocLayout::seg_keys);
+    a.seg_hdr = reinterpret_cast<uint32_t*>(base + NoAllocLayout::seg_hdr);
+    a.row_ticket = reinterpret_cast<uint32_t*>(base + NoAllocLayout::tickets);
+    a.segs = stream_segments(rows, vocabulary, device);
+    const int e = launch_stream(a, stream);
+    if (e != cudaSuccess) return cuda_fail(static_cast<cudaError_t>(e), "prepare_noalloc");
+    return ok();
+}

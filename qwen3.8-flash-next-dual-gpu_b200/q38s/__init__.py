@@ -39,6 +39,7 @@ EXPORTS = (
     "q38s_batch_reset", "q38s_batch_states", "q38s_batch_commit_tokens", "q38s_batch_prepare",
     "q38s_batch_commit", "q38s_batch_sample_commit",
     "q38s_mtp_verify", "q38s_shard_topk", "q38s_shard_merge_sample", "q38s_argmax_bf16",
+    "q38s_prepare_noalloc",
 )
 
 
