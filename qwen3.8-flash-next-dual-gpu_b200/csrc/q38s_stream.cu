@@ -42,6 +42,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 #include "q38s_kernels.cuh"
 
 namespace q38s {
@@ -57,7 +59,7 @@ constexpr uint32_t kBuf = 2048;                  // candidate buffer (rank keys)
 constexpr uint32_t kSlice = kBuf / (kCons / 32);  // candidate slice of one consumer warp
 constexpr uint32_t kShrinkAt = kSlice - 32;      // warp compaction trigger
 constexpr int kWarpPer = kSlice / 32;            // slice entries per lane
-constexpr uint32_t kStage = 64;                  // staged exact evaluations per warp round
+constexpr uint32_t kList = 64;                   // raw candidates a warp holds before evaluating
 constexpr uint32_t kFinal = kSegCap;             // candidates entering the epilogue
 constexpr uint32_t kGather = 1024;               // exact gather of the general path
 constexpr uint32_t kArea = 32768;                // candidate / epilogue work area
@@ -102,9 +104,10 @@ struct __align__(16) Ctl {
     uint32_t n_cand;
     uint32_t flags;
     uint32_t mrun;         // running maximum of exact candidate keys
+    uint32_t theta_sh;     // best top-k lower bound any warp has found
     uint32_t fail_g;       // first tile a consumer warp gave up waiting for
     uint32_t wcnt[kCons / 32];  // per-warp slice lengths at the end of a unit
-    uint32_t stage[kCons / 32][kStage];  // per-warp tile indices awaiting exact values
+    uint64_t rawlist[kCons / 32][kList];  // per-warp raw candidates awaiting exact values
     uint32_t bc_u32[4];
     uint64_t bc_u64[2];
     uint32_t red_u32[kCons / 32];
@@ -412,7 +415,7 @@ __device__ __forceinline__ bool warp_push(bool push, uint64_t key, uint64_t* buf
 }
 
 // Seed threshold from the consumers' keys (one per thread, 0 = none): the
-// largest t on the 2^8 grid with #{keys >= t} >= k, a lower bound of the
+// largest t on the 2^16 grid with #{keys >= t} >= k, a lower bound of the
 // k-th largest key (0 when k is 0 or above 256 or fewer than k keys exist);
 // *mx gets the largest key.  Warp 0 searches bit by bit with warp sums; no
 // shared-memory atomics.
@@ -432,7 +435,8 @@ __device__ uint32_t seed_select(uint32_t key, uint32_t k, uint32_t* mx, Ctl& c) 
         m = __reduce_max_sync(0xffffffffu, m);
         uint32_t t = 0;
         if (k >= 1 && k <= static_cast<uint32_t>(kCons)) {
-            for (int b = 31; b >= 8; --b) {
+#pragma unroll 1
+            for (int b = 31; b >= 16; --b) {
                 const uint32_t cand = t | (1u << b);
                 uint32_t cnt = 0;
 #pragma unroll
@@ -594,10 +598,11 @@ __device__ uint32_t finish_buffer(uint64_t* cand, uint32_t n, const Row& r, uint
 // Exact k-th largest value key among a warp's slice entries (kWarpPer per
 // lane, 0 = empty): the largest t with #{value keys >= t} >= k, found bit by
 // bit with warp sums.  Whole warp.
-__device__ __forceinline__ uint32_t warp_kth_value(const uint64_t (&e)[kWarpPer], uint32_t k) {
+__device__ __forceinline__ uint32_t warp_kth_value(const uint64_t (&e)[kWarpPer], uint32_t k,
+                                                   int low_bit = 0) {
     uint32_t t = 0;
 #pragma unroll 1
-    for (int b = 31; b >= 0; --b) {
+    for (int b = 31; b >= low_bit; --b) {
         const uint32_t cand = t | (1u << b);
         uint32_t cnt = 0;
 #pragma unroll
@@ -618,13 +623,13 @@ __device__ __forceinline__ void load_slice(const uint64_t* slice, uint32_t cnt,
     }
 }
 
-// Exact k-th largest value key of a warp's slice (cnt > k).  The k-th
-// largest of a subset of the row is at most the row's k-th largest, so it
-// is a valid threshold.  Whole warp.
+// The k-th largest value key of a warp's slice (cnt > k), rounded down to
+// its top 16 bits.  The k-th largest of a subset of the row is at most the
+// row's k-th largest, so it is a valid threshold.  Whole warp.
 __device__ __noinline__ uint32_t slice_kth(const uint64_t* slice, uint32_t cnt, uint32_t k) {
     uint64_t e[kWarpPer];
     load_slice(slice, cnt, e);
-    return warp_kth_value(e, k);
+    return warp_kth_value(e, k, 16);
 }
 
 // Keeps the slice entries whose value key is >= th; returns the new length.
@@ -1398,10 +1403,86 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
         if (tid == 0) {
             c.flags = 0;
             c.mrun = 0;
+            c.theta_sh = 0;
         }
         cbar();
         uint32_t theta = 0, cnt = 0, seen_m = 0;
+#ifdef Q38S_TRACE
+        long long tr_flush_cyc = 0;
+        uint32_t tr_flushes = 0;
+#endif
+        uint32_t nlist = 0;     // entries in this warp's raw list (warp-uniform)
+        uint32_t rawkey_w = 0;  // largest raw-value key this warp has evaluated
+        // evaluate small-k rows' lists sooner, so their top-k bound rises early
+        const uint32_t flush_at = r.k_eff ? min(32u, max(r.k_eff, 8u)) : 32u;
         bool hopeless = false, wover = false;
+        // Exact values of the warp's raw list, one entry per lane and round
+        // (sampling.cc:76-92); those at or above theta join the warp's slice,
+        // which is compacted around its k-th value when it fills.  A new
+        // maximum raises the shared running maximum and the min-p bound.
+        auto flush_list = [&]() {
+#ifdef Q38S_TRACE
+            const long long tf0 = clock64();
+#endif
+            uint32_t wmax = 0;
+            bool inf = false;
+            for (uint32_t i0 = 0; i0 < nlist; i0 += 32) {
+                const uint32_t i = i0 + lane;
+                uint32_t k = 0, tok = 0;
+                bool push = false;
+                if (i < nlist) {
+                    const uint64_t e = c.rawlist[warp][i];
+                    const uint32_t col = static_cast<uint32_t>(e >> 33);
+                    const bool pen = (e >> 32) & 1u;
+                    tok = a.col_begin + col;
+                    uint64_t count = 1;
+                    if (pen && r.freq)
+                        count = (r.counts_row ? r.counts_row[col] : 0u) + extra_count(r, tok);
+                    const float vx =
+                        exact_value(__uint_as_float(static_cast<uint32_t>(e)), pen, count, r.p);
+                    inf |= vx == INFINITY;
+                    k = float_key(vx);
+                    push = k >= theta;
+                    if (push) wmax = max(wmax, k);
+                }
+                const uint32_t pm = __ballot_sync(kFull, push);
+                if (push) {
+                    const uint32_t pos = cnt + __popc(pm & ((1u << lane) - 1u));
+                    if (pos < kSlice) slice[pos] = rank_key(k, tok);
+                }
+                cnt += __popc(pm);
+                if (cnt > kSlice) wover = true;
+                if (cnt > kShrinkAt && !wover) {
+                    // warp-local compaction around the slice's k-th value
+                    if (r.k_eff && cnt > r.k_eff)
+                        theta = max(theta, slice_kth(slice, cnt, r.k_eff));
+                    cnt = slice_compact(slice, cnt, theta);
+                    if (cnt > kShrinkAt) wover = true;
+                }
+            }
+            nlist = 0;
+            __syncwarp();
+            // the slice's exact k-th value bounds the row's k-th value from
+            // below; share it with the other warps
+            if (r.k_eff && cnt >= 2 * r.k_eff && !wover) {
+                const uint32_t kth = slice_kth(slice, cnt, r.k_eff);
+                if (kth > theta) {
+                    theta = kth;
+                    if (lane == 0) atomicMax(&c.theta_sh, kth);
+                }
+            }
+            wmax = __reduce_max_sync(kFull, wmax);
+            if (__any_sync(kFull, inf) && lane == 0) atomicOr(&c.flags, kFInf);
+            if (wmax > seen_m) {
+                seen_m = wmax;
+                if (lane == 0) atomicMax(&c.mrun, wmax);
+                if (r.minp) theta = max(theta, minp_key(wmax, r));
+            }
+#ifdef Q38S_TRACE
+            tr_flush_cyc += clock64() - tf0;
+            ++tr_flushes;
+#endif
+        };
         const unsigned char* src_row = row_ptr<DT>(a, v);
         for (uint32_t t = 0; t < ntiles; ++t, ++g) {
             const uint32_t slot = g % kRing;
@@ -1411,6 +1492,10 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             const uint32_t n = min(c1 - t0, TC);
             bool ok = !stop && wait_full(c, slot, (g / kRing) & 1u);
             ok = __all_sync(kFull, ok);
+#ifdef Q38S_TRACE
+            const long long tr_w0 = clock64();
+            uint32_t tr_looks = 0;
+#endif
             if (!ok && !stop) {
                 stop = true;
                 if (lane == 0) {
@@ -1490,6 +1575,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                         }
                     }
                 }
+                rawkey_w = __reduce_max_sync(kFull, float_key(best));
                 uint32_t m0;
                 theta = seed_select(tk, r.k_eff, &m0, c);
                 if (r.minp) theta = max(theta, minp_key(m0, r));
@@ -1498,54 +1584,55 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                 hopeless = theta <= kNegInfKey && (c1 - c0) > kBuf;
                 Q38S_TT(u, 2);
                 Q38S_TR(u, 3, (static_cast<unsigned long long>(theta) << 32) | hopeless);
-            } else if (r.minp) {
-                // the min-p bound follows the running maximum of all warps
-                const uint32_t mr = *reinterpret_cast<volatile uint32_t*>(&c.mrun);
-                if (mr > seen_m) {
-                    seen_m = mr;
-                    theta = max(theta, minp_key(mr, r));
+            } else {
+                // the other warps' top-k bound, and the min-p bound of the
+                // running maximum of all warps
+                theta = max(theta, *reinterpret_cast<volatile uint32_t*>(&c.theta_sh));
+                if (r.minp) {
+                    const uint32_t mr = *reinterpret_cast<volatile uint32_t*>(&c.mrun);
+                    if (mr > seen_m) {
+                        seen_m = mr;
+                        theta = max(theta, minp_key(mr, r));
+                    }
                 }
             }
             if (ok && !hopeless && !wover) {
                 const float th = theta <= kNegInfKey ? -INFINITY : key_float(theta);
                 const float rho = raw_bound(th, r.p.temperature);
-                bool hit;
+                // one packed maximum and compare per 16-byte vector: bit q of
+                // vhit marks a vector that may hold an element at or above rho
+                uint32_t vhit = 0;
                 if (DT == Q38S_DTYPE_BF16) {
                     const __nv_bfloat16 rb = __float2bfloat16_rd(rho);
                     const __nv_bfloat162 r2 = __halves2bfloat162(rb, rb);
-                    __nv_bfloat162 m = *reinterpret_cast<const __nv_bfloat162*>(&wv[0].x);
 #pragma unroll
                     for (int q = 0; q < kU; ++q) {
-                        m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&wv[q].x));
-                        m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&wv[q].y));
-                        m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&wv[q].z));
-                        m = __hmax2(m, *reinterpret_cast<const __nv_bfloat162*>(&wv[q].w));
+                        const __nv_bfloat162 m =
+                            __hmax2(__hmax2(*reinterpret_cast<const __nv_bfloat162*>(&wv[q].x),
+                                            *reinterpret_cast<const __nv_bfloat162*>(&wv[q].y)),
+                                    __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&wv[q].z),
+                                            *reinterpret_cast<const __nv_bfloat162*>(&wv[q].w)));
+                        if (!__hblt2(m, r2)) vhit |= 1u << q;
                     }
-                    hit = !__hblt2(m, r2);
                 } else {
-                    float m = -INFINITY;
 #pragma unroll
-                    for (int q = 0; q < kU; ++q) m = fmaxf(m, vec_max<DT>(wv[q]));
-                    hit = !(m < rho);
+                    for (int q = 0; q < kU; ++q)
+                        if (!(vec_max<DT>(wv[q]) < rho)) vhit |= 1u << q;
                 }
-                // rare path: the warp gathers every element of its part of the
-                // tile that may reach theta (raw value at or above theta's raw
-                // bound, or penalised in a row whose penalties can raise a
-                // value), stages their tile indices, evaluates them exactly
-                // one per lane, and appends those at or above theta to its
-                // slice.  Rolled loops keep the code small.
-                if (__any_sync(kFull, hit || r.nonmono)) {
-                    const uint32_t tokt = a.col_begin + t0;
-                    uint32_t look = 0;  // bit q * pv + e: element e of vector q
+                // Elements of those vectors that may reach theta (raw value at
+                // or above rho, or penalised in a row whose penalties can raise
+                // a value): bit q * pv + e of look is element e of vector q.
+                uint32_t look = 0;
+                if (vhit || r.nonmono) {
 #pragma unroll
                     for (int q = 0; q < kU; ++q) {
                         const uint32_t j = tid + q * kCons;
-                        if (j < nvec) {
-                            uint32_t penbits = 0;
-                            if (r.nonmono) {
-                                const uint32_t e0 = j * pv;
-                                penbits = (sbm[e0 >> 5] >> (e0 & 31)) & ((1u << pv) - 1u);
-                            }
+                        uint32_t penbits = 0;
+                        if (r.nonmono && j < nvec) {
+                            const uint32_t e0 = j * pv;
+                            penbits = (sbm[e0 >> 5] >> (e0 & 31)) & ((1u << pv) - 1u);
+                        }
+                        if (((vhit >> q) & 1u) || penbits) {
 #pragma unroll
                             for (int e = 0; e < static_cast<int>(pv); ++e) {
                                 const float x = vec_elem<DT>(wv[q], e);
@@ -1554,76 +1641,71 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                             }
                         }
                     }
-                    // lane offsets of the looks (inclusive warp prefix sum)
-                    const uint32_t mine = __popc(look);
-                    uint32_t incl = mine;
-#pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const uint32_t y = __shfl_up_sync(kFull, incl, o);
-                        if (lane >= static_cast<uint32_t>(o)) incl += y;
-                    }
-                    const uint32_t all = __shfl_sync(kFull, incl, 31);
-                    uint32_t* stg = c.stage[warp];
-                    uint32_t wmax = 0;
-                    bool inf = false;
-#pragma unroll 1
-                    for (uint32_t base = 0; base < all; base += kStage) {
-                        uint32_t lk = look, pos = incl - mine;
-                        while (lk) {
+                }
+                // rare path: the warp's looks go to its raw list as (raw value,
+                // column, penalised bit), one look per lane and round; the list
+                // is evaluated exactly in batches
+                if (__any_sync(kFull, look != 0)) {
+                    uint32_t lk = look, lkey = 0;
+#ifdef Q38S_TRACE
+                    const long long tq0 = clock64();
+                    tr_looks = __reduce_add_sync(kFull, __popc(look));
+#endif
+                    while (true) {
+                        const uint32_t m = __ballot_sync(kFull, lk != 0);
+                        if (!m) break;
+                        if (nlist + __popc(m) > kList) flush_list();
+                        if (lk) {
                             const uint32_t b = __ffs(lk) - 1;
                             lk &= lk - 1;
-                            if (pos >= base && pos < base + kStage)
-                                stg[pos - base] = (tid + (b / pv) * kCons) * pv + (b % pv);
-                            ++pos;
+                            const uint32_t idx = (tid + (b / pv) * kCons) * pv + (b % pv);
+                            const uint32_t pen = r.pen ? (sbm[idx >> 5] >> (idx & 31)) & 1u : 0u;
+                            const float x = load_elem<DT>(sl, idx);
+                            lkey = max(lkey, float_key(x));
+                            c.rawlist[warp][nlist + __popc(m & ((1u << lane) - 1u))] =
+                                (static_cast<uint64_t>(((t0 + idx) << 1) | pen) << 32) |
+                                __float_as_uint(x);
                         }
-                        __syncwarp();
-                        const uint32_t m = min(kStage, all - base);
-#pragma unroll 1
-                        for (uint32_t i0 = 0; i0 < m; i0 += 32) {
-                            const uint32_t i = i0 + lane;
-                            uint32_t k = 0, idx = 0;
-                            bool push = false;
-                            if (i < m) {
-                                idx = stg[i];
-                                const float vx = eval_slot(r, sbm, load_elem<DT>(sl, idx), idx,
-                                                           t0 + idx, tokt + idx);
-                                inf |= vx == INFINITY;
-                                k = float_key(vx);
-                                push = k >= theta;
-                                if (push) wmax = max(wmax, k);
-                            }
-                            const uint32_t pm = __ballot_sync(kFull, push);
-                            if (push) {
-                                const uint32_t pos2 = cnt + __popc(pm & ((1u << lane) - 1u));
-                                if (pos2 < kSlice) slice[pos2] = rank_key(k, tokt + idx);
-                            }
-                            cnt += __popc(pm);
-                            if (cnt > kSlice) wover = true;
-                            if (cnt > kShrinkAt && !wover) {
-                                // warp-local compaction around the slice's k-th value
-                                if (r.k_eff && cnt > r.k_eff)
-                                    theta = max(theta, slice_kth(slice, cnt, r.k_eff));
-                                cnt = slice_compact(slice, cnt, theta);
-                                if (cnt > kShrinkAt) wover = true;
-                            }
-                        }
+                        nlist += __popc(m);
                         __syncwarp();
                     }
-                    wmax = __reduce_max_sync(kFull, wmax);
-                    if (__any_sync(kFull, inf) && lane == 0) atomicOr(&c.flags, kFInf);
-                    if (wmax > seen_m) {
-                        seen_m = wmax;
-                        if (lane == 0) atomicMax(&c.mrun, wmax);
-                        if (r.minp) theta = max(theta, minp_key(wmax, r));
+#ifdef Q38S_TRACE
+                    const long long tq3 = clock64();
+                    if (g_trace && u < 256 && t < 20 && lane == 0)
+                        g_trace[65536 + 40960 + (static_cast<size_t>(u) * 20 + t) * 8 + warp] =
+                            static_cast<unsigned long long>(min(tq3 - tq0, 2097151ll));
+                    tr_flush_cyc = 0;
+                    tr_flushes = 0;
+#endif
+                    // a raw value above every value this warp has evaluated may
+                    // be a new row maximum: evaluate at once so the running
+                    // maximum, and with it the min-p bound, follows
+                    const uint32_t wkey = __reduce_max_sync(kFull, lkey);
+                    if (nlist && r.minp && wkey > rawkey_w) {
+                        rawkey_w = wkey;
+                        flush_list();
+                    } else if (nlist >= flush_at) {
+                        flush_list();
                     }
                 }
             }
             __syncwarp();
+#ifdef Q38S_TRACE
+            if (g_trace && u < 256 && t < 20 && lane == 0)
+                g_trace[65536 + 2 * 40960 + (static_cast<size_t>(u) * 20 + t) * 8 + warp] =
+                    (static_cast<unsigned long long>(tr_flushes) << 32) |
+                    static_cast<unsigned long long>(tr_flush_cyc);
+            if (g_trace && u < 256 && t < 20 && lane == 0)
+                g_trace[65536 + (static_cast<size_t>(u) * 20 + t) * 8 + warp] =
+                    (static_cast<unsigned long long>(tr_looks) << 32) |
+                    static_cast<unsigned long long>(clock64() - tr_w0);
+#endif
             // release the slot once every lane has read it; a slot whose
             // wait failed is never released (its copy may still land)
             if (ok && lane == 0) mbar_arrive(&c.empty[slot]);
         }
         // ---- end of unit: the warps' slices into one contiguous list
+        if (nlist && !stop && !hopeless && !wover) flush_list();
         if (lane == 0) c.wcnt[warp] = wover ? kSlice + 1 : cnt;
         const bool any_stop = cbar_or(stop);
         uint32_t total = 0, my_off = 0;
@@ -1798,7 +1880,10 @@ static int launch_stream_t(const SampleArgs& a, void* stream) {
         configured[slot][dev] = true;
     }
     const uint32_t units = a.vrows * a.segs;
-    const uint32_t cap = 2u * static_cast<uint32_t>(sms[dev]);
+    uint32_t cap = 2u * static_cast<uint32_t>(sms[dev]);
+#ifdef Q38S_TRACE
+    if (const char* gc = getenv("Q38S_TRACE_GRID")) cap = static_cast<uint32_t>(atoi(gc));
+#endif
     const uint32_t grid = units < cap ? units : cap;
     kern<<<grid, kBlock, smem, static_cast<cudaStream_t>(stream)>>>(a);
     return cudaGetLastError();
