@@ -137,6 +137,17 @@ __device__ __forceinline__ bool cbar_or(bool p) {
         : "memory");
     return r != 0;
 }
+// Number of consumer threads with p set (a barrier for all of them).
+__device__ __forceinline__ uint32_t cbar_count(bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred q;\n setp.ne.u32 q, %1, 0;\n"
+        " bar.red.popc.u32 %0, 1, 256, q;\n}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(p))
+        : "memory");
+    return r;
+}
 __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -416,42 +427,21 @@ __device__ __forceinline__ bool warp_push(bool push, uint64_t key, uint64_t* buf
 
 // Seed threshold from the consumers' keys (one per thread, 0 = none): the
 // largest t on the 2^16 grid with #{keys >= t} >= k, a lower bound of the
-// k-th largest key (0 when k is 0 or above 256 or fewer than k keys exist);
-// *mx gets the largest key.  Warp 0 searches bit by bit with warp sums; no
-// shared-memory atomics.
+// k-th largest key and hence of the row's k-th largest value (0 when k is 0
+// or above 256 or fewer than k keys exist); *mx gets the largest key.  The
+// search runs bit by bit with every thread voting through a counting
+// barrier.
 __device__ uint32_t seed_select(uint32_t key, uint32_t k, uint32_t* mx, Ctl& c) {
-    cbar();
-    c.tkey[threadIdx.x] = key;
-    cbar();
-    if (threadIdx.x < 32) {
-        const uint32_t lane = threadIdx.x;
-        uint32_t kk[kCons / 32];
-        uint32_t m = 0;
-#pragma unroll
-        for (int i = 0; i < kCons / 32; ++i) {
-            kk[i] = c.tkey[lane + 32 * i];
-            m = max(m, kk[i]);
-        }
-        m = __reduce_max_sync(0xffffffffu, m);
-        uint32_t t = 0;
-        if (k >= 1 && k <= static_cast<uint32_t>(kCons)) {
+    *mx = cmax_u32(key, c);
+    uint32_t t = 0;
+    if (k >= 1 && k <= static_cast<uint32_t>(kCons)) {
 #pragma unroll 1
-            for (int b = 31; b >= 16; --b) {
-                const uint32_t cand = t | (1u << b);
-                uint32_t cnt = 0;
-#pragma unroll
-                for (int i = 0; i < kCons / 32; ++i) cnt += kk[i] >= cand;
-                if (__reduce_add_sync(0xffffffffu, cnt) >= k) t = cand;
-            }
-        }
-        if (lane == 0) {
-            c.bc_u32[0] = t;
-            c.bc_u32[1] = m;
+        for (int b = 31; b >= 16; --b) {
+            const uint32_t cand = t | (1u << b);
+            if (cbar_count(key >= cand) >= k) t = cand;
         }
     }
-    cbar();
-    *mx = c.bc_u32[1];
-    return c.bc_u32[0];
+    return t;
 }
 
 // Exact k-th largest value key (upper 32 bits of the rank keys) among
@@ -1546,8 +1536,13 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                                                 0xff800000u));
             }
             if (t == 0) {
-                // seed (every warp takes part): exact value of each thread's
-                // largest raw logit, then the block's k-th / maximum
+#ifdef Q38S_TRACE
+                const long long ts0 = clock64();
+#endif
+                // seed (every warp takes part): a lower bound of the exact
+                // value of each thread's largest raw logit over the tiles
+                // already in the ring (up to four: about a fifth of a row),
+                // then the block's k-th / maximum
                 float best = -INFINITY;
                 int bq = -1;
 #pragma unroll
@@ -1558,8 +1553,37 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                         bq = q;
                     }
                 }
+                float ahead = -INFINITY;  // the same over the next ring tiles
+                if (ok && !r.freq) {
+#pragma unroll 1
+                    for (uint32_t t2 = 1; t2 < min(ntiles, kRing); ++t2) {
+                        const uint32_t g2 = g + t2;
+                        const uint32_t n2 = min(c1 - (t0 + t2 * TC), TC);
+                        // tiles that need consumer fix-ups are read in their own turn
+                        if (!a.use_tma || (n2 * es) % 16 != 0 || n2 % pv != 0) break;
+                        if (!wait_full(c, g2 % kRing, (g2 / kRing) & 1u)) break;
+                        const uint4* v2 = reinterpret_cast<const uint4*>(ring + (g2 % kRing) * kSlot);
+#pragma unroll
+                        for (int q = 0; q < kU; ++q) {
+                            const uint32_t j = tid + q * kCons;
+                            if (j < n2 / pv) ahead = fmaxf(ahead, vec_max<DT>(v2[j]));
+                        }
+                    }
+                }
+                if (ahead > best) {
+                    best = ahead;
+                    bq = 0;
+                }
+                // Lower bound of the exact value of the thread's largest raw
+                // logit, whatever its penalty bit: the smaller of its
+                // unpenalised and penalised values (no count is needed without
+                // a frequency penalty; those rows find the element instead).
                 uint32_t tk = 0;
-                if (ok && bq >= 0) {
+                if (ok && bq >= 0 && !r.freq) {
+                    float lb = exact_value(best, false, 1, r.p);
+                    if (r.pen) lb = fminf(lb, exact_value(best, true, 1, r.p));
+                    tk = float_key(lb);
+                } else if (ok && bq >= 0) {
                     const uint32_t j = tid + bq * kCons;
 #pragma unroll 1
                     for (uint32_t e = 0; e < pv; ++e) {
@@ -1575,10 +1599,20 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                         }
                     }
                 }
+#ifdef Q38S_TRACE
+                const long long ts1 = clock64();
+#endif
                 rawkey_w = __reduce_max_sync(kFull, float_key(best));
                 uint32_t m0;
                 theta = seed_select(tk, r.k_eff, &m0, c);
+#ifdef Q38S_TRACE
+                const long long ts2 = clock64();
+#endif
                 if (r.minp) theta = max(theta, minp_key(m0, r));
+#ifdef Q38S_TRACE
+                const long long ts3 = clock64();
+                if (tid == 0) Q38S_TR(u, 13, ((ts1 - ts0) << 42) | ((ts2 - ts1) << 21) | (ts3 - ts2));
+#endif
                 if (tid == 0) atomicMax(&c.mrun, m0);
                 seen_m = m0;
                 hopeless = theta <= kNegInfKey && (c1 - c0) > kBuf;
