@@ -54,22 +54,21 @@ constexpr uint32_t kTileBm = 1024;               // bitmap bytes per slot (8,192
 constexpr uint32_t kSlot = kTileBytes + kTileBm;
 constexpr uint32_t kRing = 4;                    // ring slots per CTA
 constexpr int kCons = 256;                       // consumer threads (warps 0-7)
-constexpr int kBlock = kCons + 32;               // + the producer warp
+constexpr int kBlock = kCons + 64;               // + the producer and the evaluator warp
 constexpr uint32_t kBuf = 2048;                  // candidate buffer (rank keys)
-constexpr uint32_t kSlice = kBuf / (kCons / 32);  // candidate slice of one consumer warp
-constexpr uint32_t kShrinkAt = kSlice - 32;      // warp compaction trigger
-constexpr int kWarpPer = kSlice / 32;            // slice entries per lane
-constexpr uint32_t kList = 64;                   // raw candidates a warp holds before evaluating
+constexpr uint32_t kQ = 512;                     // raw-candidate queue (entries)
 constexpr uint32_t kFinal = kSegCap;             // candidates entering the epilogue
 constexpr uint32_t kGather = 1024;               // exact gather of the general path
 constexpr uint32_t kArea = 32768;                // candidate / epilogue work area
 constexpr double kFix = 8796093022208.0;         // 2^43: fixed-point weight unit
 
+constexpr uint32_t kPosInfKey = 0xff800000u;      // float_key(+inf)
 constexpr uint32_t kFOverflow = 1u;
 constexpr uint32_t kFInf = 2u;
 constexpr uint32_t kFTimeout = 4u;
 
 static_assert(kBuf * 8 + kFinal * 8 + 3 * kFinal * 8 <= kArea, "fast-path area");
+static_assert(kQ <= 4 * kFinal, "the queue shares the epilogue's part of the area");
 
 // Optional per-unit trace (build with -DQ38S_TRACE; off in the product
 // build): 16 words per unit -- global-timer stamps of the unit's phases, its
@@ -103,11 +102,15 @@ struct __align__(16) Ctl {
     uint32_t issued;       // tiles issued by the producer
     uint32_t n_cand;
     uint32_t flags;
-    uint32_t mrun;         // running maximum of exact candidate keys
-    uint32_t theta_sh;     // best top-k lower bound any warp has found
+    uint32_t mrun;         // the seed's largest exact key
+    uint32_t theta_pub;    // the unit's threshold: value keys below it are never kept
     uint32_t fail_g;       // first tile a consumer warp gave up waiting for
-    uint32_t wcnt[kCons / 32];  // per-warp slice lengths at the end of a unit
-    uint64_t rawlist[kCons / 32][kList];  // per-warp raw candidates awaiting exact values
+    uint32_t q_head;       // queue entries reserved by the consumers (running count)
+    uint32_t q_tail;       // queue entries the evaluator has taken (running count)
+    uint32_t cons_done;    // consumer warps that finished their units' tiles (running count)
+#ifdef Q38S_TRACE
+    unsigned long long tr_qwait;  // consumer cycles spent waiting for queue room
+#endif
     uint32_t bc_u32[4];
     uint64_t bc_u64[2];
     uint32_t red_u32[kCons / 32];
@@ -148,6 +151,9 @@ __device__ __forceinline__ uint32_t cbar_count(bool p) {
         : "memory");
     return r;
 }
+// Named barrier 2 spans the consumers and the evaluator warp (288
+// threads): the start and the end of every unit.
+__device__ __forceinline__ void ebar() { asm volatile("bar.sync 2, 288;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -584,58 +590,55 @@ __device__ uint32_t finish_buffer(uint64_t* cand, uint32_t n, const Row& r, uint
     return r.k_eff ? min(n, r.k_eff) : n;
 }
 
-// ------------------------------------------------------ warp candidate slices
-// Exact k-th largest value key among a warp's slice entries (kWarpPer per
-// lane, 0 = empty): the largest t with #{value keys >= t} >= k, found bit by
-// bit with warp sums.  Whole warp.
-__device__ __forceinline__ uint32_t warp_kth_value(const uint64_t (&e)[kWarpPer], uint32_t k,
-                                                   int low_bit = 0) {
+// ------------------------------------------------------ evaluator buffer
+// The k-th largest value key among buf[0..n) (n >= k >= 1), rounded down to
+// its top 16 bits: the largest t on the 2^16 grid with #{value keys >= t}
+// >= k, found bit by bit with warp sums.  The k-th largest of a subset of
+// the row is at most the row's k-th largest, so it is a valid threshold.
+// One warp.
+__device__ __noinline__ uint32_t buf_kth(const uint64_t* buf, uint32_t n, uint32_t k) {
+    const uint32_t lane = threadIdx.x & 31;
     uint32_t t = 0;
+    if (n <= 512) {  // value keys in registers, 16 per lane
+        uint32_t e[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            const uint32_t i = lane + 32u * m;
+            e[m] = i < n ? static_cast<uint32_t>(buf[i] >> 32) : 0u;
+        }
 #pragma unroll 1
-    for (int b = 31; b >= low_bit; --b) {
+        for (int b = 31; b >= 16; --b) {
+            const uint32_t cand = t | (1u << b);
+            uint32_t cnt = 0;
+#pragma unroll
+            for (int m = 0; m < 16; ++m) cnt += e[m] >= cand ? 1u : 0u;
+            if (__reduce_add_sync(0xffffffffu, cnt) >= k) t = cand;
+        }
+        return t;
+    }
+#pragma unroll 1
+    for (int b = 31; b >= 16; --b) {
         const uint32_t cand = t | (1u << b);
         uint32_t cnt = 0;
-#pragma unroll
-        for (int m = 0; m < kWarpPer; ++m) cnt += static_cast<uint32_t>(e[m] >> 32) >= cand;
+        for (uint32_t i = lane; i < n; i += 32)
+            cnt += static_cast<uint32_t>(buf[i] >> 32) >= cand ? 1u : 0u;
         if (__reduce_add_sync(0xffffffffu, cnt) >= k) t = cand;
     }
     return t;
 }
 
-// A warp's slice entries (kWarpPer per lane, 0 = empty) into registers.
-__device__ __forceinline__ void load_slice(const uint64_t* slice, uint32_t cnt,
-                                           uint64_t (&e)[kWarpPer]) {
+// Keeps the entries of buf[0..n) whose value key is >= th, in place (order
+// kept); returns their number.  One warp.
+__device__ __noinline__ uint32_t buf_compact(uint64_t* buf, uint32_t n, uint32_t th) {
     const uint32_t lane = threadIdx.x & 31;
-#pragma unroll
-    for (int m = 0; m < kWarpPer; ++m) {
-        const uint32_t i = lane + 32 * m;
-        e[m] = i < cnt ? slice[i] : 0ull;
-    }
-}
-
-// The k-th largest value key of a warp's slice (cnt > k), rounded down to
-// its top 16 bits.  The k-th largest of a subset of the row is at most the
-// row's k-th largest, so it is a valid threshold.  Whole warp.
-__device__ __noinline__ uint32_t slice_kth(const uint64_t* slice, uint32_t cnt, uint32_t k) {
-    uint64_t e[kWarpPer];
-    load_slice(slice, cnt, e);
-    return warp_kth_value(e, k, 16);
-}
-
-// Keeps the slice entries whose value key is >= th; returns the new length.
-// Whole warp.
-__device__ __noinline__ uint32_t slice_compact(uint64_t* slice, uint32_t cnt, uint32_t th) {
-    const uint32_t lane = threadIdx.x & 31;
-    uint64_t e[kWarpPer];
-    load_slice(slice, cnt, e);
-    __syncwarp();
     uint32_t out = 0;
-#pragma unroll
-    for (int m = 0; m < kWarpPer; ++m) {
-        const bool keep = e[m] != 0ull && static_cast<uint32_t>(e[m] >> 32) >= th;
-        const uint32_t mask = __ballot_sync(0xffffffffu, keep);
-        if (keep) slice[out + __popc(mask & ((1u << lane) - 1u))] = e[m];
-        out += __popc(mask);
+    for (uint32_t i0 = 0; i0 < n; i0 += 32) {
+        const uint32_t i = i0 + lane;
+        const uint64_t e = i < n ? buf[i] : 0ull;
+        const bool keep = i < n && static_cast<uint32_t>(e >> 32) >= th;
+        const uint32_t m = __ballot_sync(0xffffffffu, keep);
+        if (keep) buf[out + __popc(m & ((1u << lane) - 1u))] = e;
+        out += __popc(m);
     }
     __syncwarp();
     return out;
@@ -1282,6 +1285,7 @@ __device__ __forceinline__ void chunk_range(uint32_t vocab, uint32_t S, uint32_t
 }
 
 __device__ bool wait_full(Ctl& c, uint32_t slot, uint32_t phase) {
+    if (mbar_try_wait(&c.full[slot], phase)) return true;
     const long long start = clock64();
     while (!mbar_try_wait(&c.full[slot], phase)) {
         if (*reinterpret_cast<volatile uint32_t*>(&c.abort_flag)) return false;
@@ -1338,6 +1342,230 @@ __device__ void produce(const SampleArgs& a, unsigned char* ring, Ctl& c) {
     atomicExch(&c.prod_done, 1u);
 }
 
+// Evaluator (warp 9): takes the raw candidates the consumers queue, in
+// queue order, 32 per round; gives each its exact value (sampling.cc:76-92)
+// and keeps those at or above theta in the unit's candidate buffer as rank
+// keys.  theta is the best lower bound known of the smallest value the row
+// can keep: the seed's, the k-th largest buffered value and, for min-p
+// rows, M + ln(min_p) - slack with M the largest exact value seen.  Every
+// rise is published to the consumers, whose filter uses it from their next
+// tile on.
+//
+// The k-th largest buffered value is tracked with a 256-bin histogram of
+// value keys laid out from the seed's threshold up to twice the seed's
+// maximum (higher keys count in the top bin): after every round the lower
+// edge of the highest bin at which the count from the top reaches k is a
+// lower bound of the k-th largest buffered value.  Without a seed threshold
+// (top_k above 256) a bit search over the buffer refreshes it instead as
+// the buffer grows.
+//
+// Queue protocol: an entry is 1 << 63 | ((column << 1) | penalised) << 32 |
+// raw value bits; 0 marks a free slot.  A consumer warp reserves up to 32
+// slots at a time on q_head and waits until q_tail leaves room; the
+// evaluator takes the contiguous written prefix, clears it and advances
+// q_tail.  The oldest reservation always has room (it is at most 32 of kQ
+// slots), so every wait ends.
+template <int DT>
+__device__ void evaluate(const SampleArgs& a, unsigned char* area, Ctl& c) {
+    constexpr unsigned kFull = 0xffffffffu;
+    const uint32_t lane = threadIdx.x & 31;
+    uint64_t* buf = reinterpret_cast<uint64_t*>(area);
+    volatile uint64_t* q = reinterpret_cast<volatile uint64_t*>(buf + kBuf);
+    uint32_t* hist = c.hist;
+    const uint32_t S = a.segs;
+    const uint32_t n_units = a.vrows * S;
+    uint32_t tail = 0;     // queue entries taken (all units of this CTA)
+    uint32_t done_at = 0;  // consumer-warp completions that end the unit
+    for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+        Row r;
+        load_row(a, u / S, r);
+        done_at += kCons / 32;
+        ebar();  // unit start: shared words reset, queue cleared
+#pragma unroll
+        for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
+        uint32_t theta = 0, pub = 0, mx = 0, n = 0, flags = 0;
+        const uint32_t step = r.k_eff ? max(16u, r.k_eff / 4) : 0u;
+        uint32_t kth_at = r.k_eff ? r.k_eff + step : 0xffffffffu;
+        bool over = false, hist_on = false;
+        uint32_t hbase = 0, hshift = 0;
+        long long idle0 = clock64();
+#ifdef Q38S_TRACE
+        uint32_t tr_entries = 0, tr_rounds = 0, tr_kth = 0;
+        long long tr_kcyc = 0;
+#endif
+        while (true) {
+            const uint64_t e = q[(tail + lane) % kQ];
+            const uint32_t vm = __ballot_sync(kFull, (e >> 63) != 0);
+            const uint32_t run = vm == kFull ? 32u : static_cast<uint32_t>(__ffs(~vm) - 1);
+            if (run == 0) {
+                const uint32_t cd = *reinterpret_cast<volatile uint32_t*>(&c.cons_done);
+                if (static_cast<int32_t>(cd - done_at) >= 0) {
+                    // every consumer warp has queued its last entry
+                    __threadfence_block();
+                    const uint32_t head = *reinterpret_cast<volatile uint32_t*>(&c.q_head);
+                    if (head == tail || *reinterpret_cast<volatile uint32_t*>(&c.abort_flag)) break;
+                }
+                if (clock64() - idle0 > 2 * kWaitLimitCycles) {
+                    flags |= kFTimeout;
+                    if (lane == 0) atomicOr(&c.abort_flag, 1u);
+                    break;
+                }
+                __nanosleep(64);  // leave the issue slots to the consumers
+                continue;
+            }
+            idle0 = clock64();
+#ifdef Q38S_TRACE
+            tr_entries += run;
+            ++tr_rounds;
+#endif
+            // the seed's bounds (published once per unit by the consumers)
+            {
+                const uint32_t ts = *reinterpret_cast<volatile uint32_t*>(&c.theta_pub);
+                const uint32_t ms = *reinterpret_cast<volatile uint32_t*>(&c.mrun);
+                theta = max(theta, ts);
+                if (ms > mx) {
+                    mx = ms;
+                    if (r.minp) theta = max(theta, minp_key(mx, r));
+                }
+                if (!hist_on && r.k_eff && ts >= 0x10000u) {
+                    // bins from the seed threshold up to twice the seed maximum
+                    hist_on = true;
+                    hbase = ts & 0xffff0000u;
+                    const uint32_t range = max(ms, hbase) - hbase;
+                    while ((range >> hshift) >= 128u) ++hshift;
+                }
+            }
+            uint32_t k = 0, tok = 0;
+            bool inf = false;
+            if (lane < run) {
+                q[(tail + lane) % kQ] = 0ull;
+                if (!over) {
+                    const uint32_t col = static_cast<uint32_t>(e >> 33) & 0x3fffffffu;
+                    const bool pen = (e >> 32) & 1u;
+                    tok = a.col_begin + col;
+                    uint64_t count = 1;
+                    if (pen && r.freq)
+                        count = (r.counts_row ? r.counts_row[col] : 0u) + extra_count(r, tok);
+                    const float vx =
+                        transform(__uint_as_float(static_cast<uint32_t>(e)), pen, count, r.p);
+                    inf = vx == INFINITY;
+                    k = float_key(vx);
+                }
+            }
+            tail += run;
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();  // the cleared slots before the new tail
+                *reinterpret_cast<volatile uint32_t*>(&c.q_tail) = tail;
+            }
+            if (over) continue;
+            if (__any_sync(kFull, inf)) flags |= kFInf;
+            const uint32_t bm = __reduce_max_sync(kFull, k);
+            if (bm > mx) {
+                mx = bm;
+                if (r.minp) theta = max(theta, minp_key(mx, r));
+            }
+            bool push = lane < run && k >= theta;
+            if (n + 32 > kBuf && __any_sync(kFull, push)) {
+                // full: compact around the k-th value and theta
+                if (r.k_eff && n > r.k_eff) theta = max(theta, buf_kth(buf, n, r.k_eff));
+                n = buf_compact(buf, n, theta);
+                push = push && k >= theta;
+                if (n + 32 > kBuf) {
+                    // overflow: the row takes the general path; a threshold
+                    // of +inf stops the consumers' queueing
+                    over = true;
+                    flags |= kFOverflow;
+                    if (lane == 0) atomicMax(&c.theta_pub, kPosInfKey);
+                    continue;
+                }
+            }
+            const uint32_t pm = __ballot_sync(kFull, push);
+            if (push) {
+                buf[n + __popc(pm & ((1u << lane) - 1u))] = rank_key(k, tok);
+                if (hist_on) atomicAdd(&hist[min((k - hbase) >> hshift, 255u)], 1u);
+            }
+            n += __popc(pm);
+            if (hist_on) {
+                if (pm) {
+                    __syncwarp();
+                    // highest bin at which the count from the top reaches k
+                    uint32_t h[8], s8 = 0;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        h[j] = hist[255 - 8 * lane - j];
+                        s8 += h[j];
+                    }
+                    uint32_t inc = s8;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const uint32_t y = __shfl_up_sync(kFull, inc, o);
+                        if (lane >= static_cast<uint32_t>(o)) inc += y;
+                    }
+                    const uint32_t hit = __ballot_sync(kFull, inc >= r.k_eff);
+                    if (hit) {
+                        const uint32_t L = __ffs(hit) - 1;
+                        uint32_t bin = 0;
+                        if (lane == L) {
+                            uint32_t acc = inc - s8;
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                acc += h[j];
+                                if (acc >= r.k_eff) {
+                                    bin = 255 - 8 * lane - j;
+                                    break;
+                                }
+                            }
+                        }
+                        bin = __shfl_sync(kFull, bin, L);
+                        theta = max(theta, hbase + (bin << hshift));
+                    }
+                }
+            } else if (n >= kth_at) {
+#ifdef Q38S_TRACE
+                const long long tk0 = clock64();
+                ++tr_kth;
+#endif
+                __syncwarp();
+                theta = max(theta, buf_kth(buf, n, r.k_eff));
+                n = buf_compact(buf, n, theta);
+                kth_at = n + step;
+#ifdef Q38S_TRACE
+                tr_kcyc += clock64() - tk0;
+#endif
+            }
+            if (theta > pub) {
+                pub = theta;
+                if (lane == 0) atomicMax(&c.theta_pub, theta);
+            }
+#ifdef Q38S_TRACE
+            if (g_trace && lane == 0 && u < 256 && tr_rounds <= 32)
+                g_trace[106496 + static_cast<size_t>(u) * 32 + tr_rounds - 1] =
+                    ((gtime() & 0xffffffffull) << 32) | theta;
+#endif
+        }
+        tail = *reinterpret_cast<volatile uint32_t*>(&c.q_head);
+        // drop what the final threshold excludes
+        if (!over && n) n = buf_compact(buf, n, theta);
+#ifdef Q38S_TRACE
+        if (g_trace && lane == 0 && u < 8192) {
+            g_trace[static_cast<size_t>(u) * 16 + 10] = gtime();
+            g_trace[static_cast<size_t>(u) * 16 + 14] =
+                (static_cast<unsigned long long>(tr_entries) << 32) | tr_rounds;
+            g_trace[static_cast<size_t>(u) * 16 + 15] =
+                (static_cast<unsigned long long>(tr_kth) << 32) |
+                static_cast<unsigned long long>(min(tr_kcyc, 0xffffffffll));
+        }
+#endif
+        if (lane == 0) {
+            c.n_cand = over ? 0u : n;
+            if (flags) atomicOr(&c.flags, flags);
+        }
+        __syncwarp();
+        ebar();  // unit end: the consumers finish from the buffer
+    }
+}
+
 template <int DT>
 __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
     extern __shared__ __align__(1024) unsigned char dsm[];
@@ -1362,25 +1590,31 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
         c.prod_done = 0;
         c.issued = 0;
         c.fail_g = 0xffffffffu;
+        c.q_head = 0;
+        c.q_tail = 0;
+        c.cons_done = 0;
         fence_mbar_init();
     }
     __syncthreads();
+    if (tid >= static_cast<uint32_t>(kCons + 32)) {
+        evaluate<DT>(a, area, c);
+        return;
+    }
     if (tid >= static_cast<uint32_t>(kCons)) {
         if (tid == static_cast<uint32_t>(kCons)) produce<DT>(a, ring, c);
         return;
     }
 
     // Consumers.  Inside a unit the warps run decoupled: each waits for and
-    // releases the slots itself, keeps its own threshold and pushes its
-    // candidates into its own slice of the buffer (a register counter, no
-    // shared atomics).  Block barriers: the seed (once per unit), rare tile
-    // fix-ups, and the end of the unit.
+    // releases the slots itself and queues the few elements its filter lets
+    // through for the evaluator warp.  Block barriers: the seed (once per
+    // unit), rare tile fix-ups, and the start and end of the unit.
     const uint32_t warp = tid >> 5, lane = tid & 31;
-    uint64_t* slice = cand + warp * kSlice;
+    uint64_t* qbuf = cand + kBuf;  // the raw-candidate queue
     const uint32_t S = a.segs;
     const uint32_t n_units = a.vrows * S;
     uint32_t g = 0;     // tiles passed (the producer's order)
-    bool stop = false;  // this warp gave up on a copy (warp-uniform)
+    bool stop = false;  // this warp gave up on a copy or a queue slot (warp-uniform)
     for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
         const uint32_t v = u / S, seg = u % S;
         uint32_t c0, c1;
@@ -1393,86 +1627,18 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
         if (tid == 0) {
             c.flags = 0;
             c.mrun = 0;
-            c.theta_sh = 0;
+            c.theta_pub = 0;
+#ifdef Q38S_TRACE
+            c.tr_qwait = 0;
+#endif
         }
-        cbar();
-        uint32_t theta = 0, cnt = 0, seen_m = 0;
-#ifdef Q38S_TRACE
-        long long tr_flush_cyc = 0;
-        uint32_t tr_flushes = 0;
-#endif
-        uint32_t nlist = 0;     // entries in this warp's raw list (warp-uniform)
-        uint32_t rawkey_w = 0;  // largest raw-value key this warp has evaluated
-        // evaluate small-k rows' lists sooner, so their top-k bound rises early
-        const uint32_t flush_at = r.k_eff ? min(32u, max(r.k_eff, 8u)) : 32u;
-        bool hopeless = false, wover = false;
-        // Exact values of the warp's raw list, one entry per lane and round
-        // (sampling.cc:76-92); those at or above theta join the warp's slice,
-        // which is compacted around its k-th value when it fills.  A new
-        // maximum raises the shared running maximum and the min-p bound.
-        auto flush_list = [&]() {
-#ifdef Q38S_TRACE
-            const long long tf0 = clock64();
-#endif
-            uint32_t wmax = 0;
-            bool inf = false;
-            for (uint32_t i0 = 0; i0 < nlist; i0 += 32) {
-                const uint32_t i = i0 + lane;
-                uint32_t k = 0, tok = 0;
-                bool push = false;
-                if (i < nlist) {
-                    const uint64_t e = c.rawlist[warp][i];
-                    const uint32_t col = static_cast<uint32_t>(e >> 33);
-                    const bool pen = (e >> 32) & 1u;
-                    tok = a.col_begin + col;
-                    uint64_t count = 1;
-                    if (pen && r.freq)
-                        count = (r.counts_row ? r.counts_row[col] : 0u) + extra_count(r, tok);
-                    const float vx =
-                        exact_value(__uint_as_float(static_cast<uint32_t>(e)), pen, count, r.p);
-                    inf |= vx == INFINITY;
-                    k = float_key(vx);
-                    push = k >= theta;
-                    if (push) wmax = max(wmax, k);
-                }
-                const uint32_t pm = __ballot_sync(kFull, push);
-                if (push) {
-                    const uint32_t pos = cnt + __popc(pm & ((1u << lane) - 1u));
-                    if (pos < kSlice) slice[pos] = rank_key(k, tok);
-                }
-                cnt += __popc(pm);
-                if (cnt > kSlice) wover = true;
-                if (cnt > kShrinkAt && !wover) {
-                    // warp-local compaction around the slice's k-th value
-                    if (r.k_eff && cnt > r.k_eff)
-                        theta = max(theta, slice_kth(slice, cnt, r.k_eff));
-                    cnt = slice_compact(slice, cnt, theta);
-                    if (cnt > kShrinkAt) wover = true;
-                }
-            }
-            nlist = 0;
-            __syncwarp();
-            // the slice's exact k-th value bounds the row's k-th value from
-            // below; share it with the other warps
-            if (r.k_eff && cnt >= 2 * r.k_eff && !wover) {
-                const uint32_t kth = slice_kth(slice, cnt, r.k_eff);
-                if (kth > theta) {
-                    theta = kth;
-                    if (lane == 0) atomicMax(&c.theta_sh, kth);
-                }
-            }
-            wmax = __reduce_max_sync(kFull, wmax);
-            if (__any_sync(kFull, inf) && lane == 0) atomicOr(&c.flags, kFInf);
-            if (wmax > seen_m) {
-                seen_m = wmax;
-                if (lane == 0) atomicMax(&c.mrun, wmax);
-                if (r.minp) theta = max(theta, minp_key(wmax, r));
-            }
-#ifdef Q38S_TRACE
-            tr_flush_cyc += clock64() - tf0;
-            ++tr_flushes;
-#endif
-        };
+        // the queue shares the area with the previous unit's epilogue
+        for (uint32_t i = tid; i < kQ; i += kCons) qbuf[i] = 0ull;
+        ebar();
+        uint32_t theta = 0;
+        uint32_t rho_theta = 1;  // the threshold rho was derived from (1: none yet)
+        float rho = 0.0f;        // raw-logit bound of theta
+        bool hopeless = false;
         const unsigned char* src_row = row_ptr<DT>(a, v);
         for (uint32_t t = 0; t < ntiles; ++t, ++g) {
             const uint32_t slot = g % kRing;
@@ -1480,12 +1646,14 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             uint32_t* sbm = reinterpret_cast<uint32_t*>(sl + kTileBytes);
             const uint32_t t0 = c0 + t * TC;
             const uint32_t n = min(c1 - t0, TC);
-            bool ok = !stop && wait_full(c, slot, (g / kRing) & 1u);
-            ok = __all_sync(kFull, ok);
 #ifdef Q38S_TRACE
-            const long long tr_w0 = clock64();
-            uint32_t tr_looks = 0;
+            const long long tw0 = clock64();
 #endif
+            bool ok = !stop && wait_full(c, slot, (g / kRing) & 1u);
+#ifdef Q38S_TRACE
+            const long long tw1 = clock64();
+#endif
+            ok = __all_sync(kFull, ok);
             if (!ok && !stop) {
                 stop = true;
                 if (lane == 0) {
@@ -1602,7 +1770,6 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
 #ifdef Q38S_TRACE
                 const long long ts1 = clock64();
 #endif
-                rawkey_w = __reduce_max_sync(kFull, float_key(best));
                 uint32_t m0;
                 theta = seed_select(tk, r.k_eff, &m0, c);
 #ifdef Q38S_TRACE
@@ -1613,26 +1780,23 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                 const long long ts3 = clock64();
                 if (tid == 0) Q38S_TR(u, 13, ((ts1 - ts0) << 42) | ((ts2 - ts1) << 21) | (ts3 - ts2));
 #endif
-                if (tid == 0) atomicMax(&c.mrun, m0);
-                seen_m = m0;
+                if (tid == 0) {
+                    atomicMax(&c.mrun, m0);
+                    atomicMax(&c.theta_pub, theta);
+                }
                 hopeless = theta <= kNegInfKey && (c1 - c0) > kBuf;
                 Q38S_TT(u, 2);
                 Q38S_TR(u, 3, (static_cast<unsigned long long>(theta) << 32) | hopeless);
             } else {
-                // the other warps' top-k bound, and the min-p bound of the
-                // running maximum of all warps
-                theta = max(theta, *reinterpret_cast<volatile uint32_t*>(&c.theta_sh));
-                if (r.minp) {
-                    const uint32_t mr = *reinterpret_cast<volatile uint32_t*>(&c.mrun);
-                    if (mr > seen_m) {
-                        seen_m = mr;
-                        theta = max(theta, minp_key(mr, r));
-                    }
-                }
+                // the evaluator's threshold
+                theta = max(theta, *reinterpret_cast<volatile uint32_t*>(&c.theta_pub));
             }
-            if (ok && !hopeless && !wover) {
-                const float th = theta <= kNegInfKey ? -INFINITY : key_float(theta);
-                const float rho = raw_bound(th, r.p.temperature);
+            if (ok && !hopeless) {
+                if (theta != rho_theta) {
+                    rho_theta = theta;
+                    const float th = theta <= kNegInfKey ? -INFINITY : key_float(theta);
+                    rho = raw_bound(th, r.p.temperature);
+                }
                 // one packed maximum and compare per 16-byte vector: bit q of
                 // vhit marks a vector that may hold an element at or above rho
                 uint32_t vhit = 0;
@@ -1676,97 +1840,81 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                         }
                     }
                 }
-                // rare path: the warp's looks go to its raw list as (raw value,
-                // column, penalised bit), one look per lane and round; the list
-                // is evaluated exactly in batches
-                if (__any_sync(kFull, look != 0)) {
-                    uint32_t lk = look, lkey = 0;
 #ifdef Q38S_TRACE
-                    const long long tq0 = clock64();
-                    tr_looks = __reduce_add_sync(kFull, __popc(look));
+                if (g_trace && u < 256 && t < 20) {
+                    const uint32_t nl = __reduce_add_sync(kFull, __popc(look));
+                    if (lane == 0)
+                        g_trace[65536 + (static_cast<size_t>(u) * 20 + t) * 8 + warp] =
+                            (static_cast<unsigned long long>(theta) << 32) | nl;
+                    if (lane == 0 && warp == 0)
+                        g_trace[114688 + static_cast<size_t>(u) * 20 + t] = gtime();
+                }
 #endif
-                    while (true) {
-                        const uint32_t m = __ballot_sync(kFull, lk != 0);
-                        if (!m) break;
-                        if (nlist + __popc(m) > kList) flush_list();
-                        if (lk) {
-                            const uint32_t b = __ffs(lk) - 1;
-                            lk &= lk - 1;
-                            const uint32_t idx = (tid + (b / pv) * kCons) * pv + (b % pv);
-                            const uint32_t pen = r.pen ? (sbm[idx >> 5] >> (idx & 31)) & 1u : 0u;
-                            const float x = load_elem<DT>(sl, idx);
-                            lkey = max(lkey, float_key(x));
-                            c.rawlist[warp][nlist + __popc(m & ((1u << lane) - 1u))] =
-                                (static_cast<uint64_t>(((t0 + idx) << 1) | pen) << 32) |
-                                __float_as_uint(x);
+                // rare path: the looks go to the evaluator's queue as (raw
+                // value, column, penalised bit), at most one per lane and round
+                while (__any_sync(kFull, look != 0)) {
+                    const uint32_t m = __ballot_sync(kFull, look != 0);
+                    uint32_t base = 0, fail = 0;
+                    if (lane == 0) {
+                        const uint32_t need = __popc(m);
+                        base = atomicAdd(&c.q_head, need);
+                        const long long w0 = clock64();
+                        while (base + need - *reinterpret_cast<volatile uint32_t*>(&c.q_tail) > kQ) {
+                            if (*reinterpret_cast<volatile uint32_t*>(&c.abort_flag) ||
+                                clock64() - w0 > kWaitLimitCycles) {
+                                fail = 1;
+                                break;
+                            }
                         }
-                        nlist += __popc(m);
-                        __syncwarp();
-                    }
 #ifdef Q38S_TRACE
-                    const long long tq3 = clock64();
-                    if (g_trace && u < 256 && t < 20 && lane == 0)
-                        g_trace[65536 + 40960 + (static_cast<size_t>(u) * 20 + t) * 8 + warp] =
-                            static_cast<unsigned long long>(min(tq3 - tq0, 2097151ll));
-                    tr_flush_cyc = 0;
-                    tr_flushes = 0;
+                        atomicAdd(&c.tr_qwait, static_cast<unsigned long long>(clock64() - w0));
 #endif
-                    // a raw value above every value this warp has evaluated may
-                    // be a new row maximum: evaluate at once so the running
-                    // maximum, and with it the min-p bound, follows
-                    const uint32_t wkey = __reduce_max_sync(kFull, lkey);
-                    if (nlist && r.minp && wkey > rawkey_w) {
-                        rawkey_w = wkey;
-                        flush_list();
-                    } else if (nlist >= flush_at) {
-                        flush_list();
+                        __threadfence_block();  // the evaluator's clears before our entries
+                    }
+                    base = __shfl_sync(kFull, base, 0);
+                    if (__shfl_sync(kFull, fail, 0)) {
+                        stop = true;
+                        if (lane == 0) atomicOr(&c.abort_flag, 1u);
+                        break;
+                    }
+                    if (look) {
+                        const uint32_t b = __ffs(look) - 1;
+                        look &= look - 1;
+                        const uint32_t idx = (tid + (b / pv) * kCons) * pv + (b % pv);
+                        const uint32_t pen = r.pen ? (sbm[idx >> 5] >> (idx & 31)) & 1u : 0u;
+                        const float x = load_elem<DT>(sl, idx);
+                        reinterpret_cast<volatile uint64_t*>(qbuf)[(base + __popc(m & ((1u << lane) - 1u))) % kQ] =
+                            (1ull << 63) |
+                            (static_cast<uint64_t>(((t0 + idx) << 1) | pen) << 32) |
+                            __float_as_uint(x);
                     }
                 }
             }
             __syncwarp();
-#ifdef Q38S_TRACE
-            if (g_trace && u < 256 && t < 20 && lane == 0)
-                g_trace[65536 + 2 * 40960 + (static_cast<size_t>(u) * 20 + t) * 8 + warp] =
-                    (static_cast<unsigned long long>(tr_flushes) << 32) |
-                    static_cast<unsigned long long>(tr_flush_cyc);
-            if (g_trace && u < 256 && t < 20 && lane == 0)
-                g_trace[65536 + (static_cast<size_t>(u) * 20 + t) * 8 + warp] =
-                    (static_cast<unsigned long long>(tr_looks) << 32) |
-                    static_cast<unsigned long long>(clock64() - tr_w0);
-#endif
             // release the slot once every lane has read it; a slot whose
             // wait failed is never released (its copy may still land)
+#ifdef Q38S_TRACE
+            if (g_trace && u < 256 && t < 20 && lane == 0 && warp == 0)
+                g_trace[119808 + static_cast<size_t>(u) * 20 + t] =
+                    (static_cast<unsigned long long>(tw1 - tw0) << 32) |
+                    static_cast<unsigned long long>(clock64() - tw1);
+#endif
             if (ok && lane == 0) mbar_arrive(&c.empty[slot]);
         }
-        // ---- end of unit: the warps' slices into one contiguous list
-        if (nlist && !stop && !hopeless && !wover) flush_list();
-        if (lane == 0) c.wcnt[warp] = wover ? kSlice + 1 : cnt;
+        // ---- end of unit: every queued entry is written; the evaluator
+        // drains the queue and leaves the candidates in cand[0..n)
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            atomicAdd(&c.cons_done, 1u);
+        }
         const bool any_stop = cbar_or(stop);
-        uint32_t total = 0, my_off = 0;
-        bool over = false;
-#pragma unroll
-        for (uint32_t w2 = 0; w2 < kCons / 32; ++w2) {
-            const uint32_t cw = c.wcnt[w2];
-            over |= cw > kSlice;
-            const uint32_t len = min(cw, kSlice);
-            if (w2 < warp) my_off += len;
-            total += len;
-        }
-        if (!over && !hopeless && !any_stop) {
-            uint64_t e[kWarpPer];
-            load_slice(slice, cnt, e);
-            cbar();
-#pragma unroll
-            for (int m = 0; m < kWarpPer; ++m) {
-                const uint32_t i = lane + 32 * m;
-                if (i < cnt) cand[my_off + i] = e[m];
-            }
-        }
-        cbar();
+        ebar();
         uint32_t flags = c.flags;
-        const uint32_t n = total;
+        const uint32_t n = c.n_cand;
+        Q38S_TR(u, 6, c.tr_qwait);
         if (any_stop) flags |= kFTimeout;
-        if (hopeless || over) flags |= kFOverflow;
+        if (hopeless) flags |= kFOverflow;
         if (a.mode == kModeShardTopK) flags &= ~kFInf;
         Q38S_TT(u, 4);
         Q38S_TR(u, 5, (static_cast<unsigned long long>(flags) << 32) | n);
