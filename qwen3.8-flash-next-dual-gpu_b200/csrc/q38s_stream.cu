@@ -50,25 +50,21 @@ namespace q38s {
 namespace {
 
 constexpr uint32_t kTileBytes = 16384;           // logits per ring slot
-constexpr uint32_t kTileBm = 1024;               // bitmap bytes per slot (8,192 columns)
-constexpr uint32_t kSlot = kTileBytes + kTileBm;
+constexpr uint32_t kSlot = kTileBytes;
 constexpr uint32_t kRing = 4;                    // ring slots per CTA
 constexpr int kCons = 256;                       // consumer threads (warps 0-7)
-constexpr int kBlock = kCons + 64;               // + the producer and the evaluator warp
+constexpr int kBlock = kCons + 32;               // + the producer warp
 constexpr uint32_t kBuf = 2048;                  // candidate buffer (rank keys)
-constexpr uint32_t kQ = 512;                     // raw-candidate queue (entries)
 constexpr uint32_t kFinal = kSegCap;             // candidates entering the epilogue
 constexpr uint32_t kGather = 1024;               // exact gather of the general path
 constexpr uint32_t kArea = 32768;                // candidate / epilogue work area
 constexpr double kFix = 8796093022208.0;         // 2^43: fixed-point weight unit
 
-constexpr uint32_t kPosInfKey = 0xff800000u;      // float_key(+inf)
 constexpr uint32_t kFOverflow = 1u;
 constexpr uint32_t kFInf = 2u;
 constexpr uint32_t kFTimeout = 4u;
 
 static_assert(kBuf * 8 + kFinal * 8 + 3 * kFinal * 8 <= kArea, "fast-path area");
-static_assert(kQ <= 4 * kFinal, "the queue shares the epilogue's part of the area");
 
 // Optional per-unit trace (build with -DQ38S_TRACE; off in the product
 // build): 16 words per unit -- global-timer stamps of the unit's phases, its
@@ -102,15 +98,7 @@ struct __align__(16) Ctl {
     uint32_t issued;       // tiles issued by the producer
     uint32_t n_cand;
     uint32_t flags;
-    uint32_t mrun;         // the seed's largest exact key
-    uint32_t theta_pub;    // the unit's threshold: value keys below it are never kept
     uint32_t fail_g;       // first tile a consumer warp gave up waiting for
-    uint32_t q_head;       // queue entries reserved by the consumers (running count)
-    uint32_t q_tail;       // queue entries the evaluator has taken (running count)
-    uint32_t cons_done;    // consumer warps that finished their units' tiles (running count)
-#ifdef Q38S_TRACE
-    unsigned long long tr_qwait;  // consumer cycles spent waiting for queue room
-#endif
     uint32_t bc_u32[4];
     uint64_t bc_u64[2];
     uint32_t red_u32[kCons / 32];
@@ -140,20 +128,6 @@ __device__ __forceinline__ bool cbar_or(bool p) {
         : "memory");
     return r != 0;
 }
-// Number of consumer threads with p set (a barrier for all of them).
-__device__ __forceinline__ uint32_t cbar_count(bool p) {
-    uint32_t r;
-    asm volatile(
-        "{\n .reg .pred q;\n setp.ne.u32 q, %1, 0;\n"
-        " bar.red.popc.u32 %0, 1, 256, q;\n}"
-        : "=r"(r)
-        : "r"(static_cast<uint32_t>(p))
-        : "memory");
-    return r;
-}
-// Named barrier 2 spans the consumers and the evaluator warp (288
-// threads): the start and the end of every unit.
-__device__ __forceinline__ void ebar() { asm volatile("bar.sync 2, 288;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -324,25 +298,76 @@ __device__ __forceinline__ float vec_max(const uint4& w) {
                  fmaxf(__uint_as_float(w.z), __uint_as_float(w.w)));
 }
 
-// Exact transformed value of a tile element (sampling.cc:76-92): the
-// penalised bit comes from the slot's bitmap copy (which carries this
-// call's additional tokens), the frequency count from global memory.  One
-// out-of-line copy of the IEEE division sequences keeps them out of the
-// unrolled streaming loop, so a warp that takes this (rare) path does not
-// miss in the instruction cache.
+// Exact transformed value (sampling.cc:76-92), one out-of-line copy of the
+// IEEE division sequences for the general path's loop.
 __device__ __noinline__ float exact_value(float x, bool penalized, uint64_t count, RowParams p) {
     return transform(x, penalized, count, p);
 }
-__device__ __forceinline__ float eval_slot(const Row& r, const uint32_t* bm, float x, uint32_t idx,
-                                           uint32_t col, uint32_t tok) {
+
+// Exact transformed value of column col given the state row's bitmap word
+// holding it (sampling.cc:76-92): the penalised bit, or membership in this
+// call's additional tokens; the frequency count from global memory.
+__device__ __forceinline__ float exact_pw(const SampleArgs& a, const Row& r, float x, uint32_t col,
+                                          uint32_t pw) {
     bool penalized = false;
     uint64_t count = 1;
     if (r.pen) {
-        penalized = (bm[idx >> 5] >> (idx & 31)) & 1u;
-        if (penalized && r.freq)
-            count = (r.counts_row ? r.counts_row[col] : 0u) + extra_count(r, tok);
+        const uint32_t tok = a.col_begin + col;
+        const uint64_t ex = r.n_extra ? extra_count(r, tok) : 0u;
+        penalized = ((pw >> (col & 31)) & 1u) || ex != 0;
+        if (penalized && r.freq) count = (r.counts_row ? r.counts_row[col] : 0u) + ex;
     }
     return exact_value(x, penalized, count, r.p);
+}
+
+// Element col of a row, from global memory.
+template <int DT>
+__device__ __forceinline__ float elem_at(const unsigned char* row, uint32_t col) {
+    if (DT == Q38S_DTYPE_BF16)
+        return __uint_as_float(static_cast<uint32_t>(
+                                   __ldg(reinterpret_cast<const uint16_t*>(row) + col)) << 16);
+    return __ldg(reinterpret_cast<const float*>(row) + col);
+}
+
+// The 16-byte vector of a row at column col0 (a multiple of its element
+// count), from global memory; elements nv and up read as -inf.
+template <int DT>
+__device__ __forceinline__ uint4 load_vec(const SampleArgs& a, const unsigned char* row,
+                                          uint32_t col0, uint32_t nv) {
+    constexpr uint32_t es = DT == Q38S_DTYPE_BF16 ? 2u : 4u;
+    constexpr uint32_t pv = 16u / es;
+    if (a.use_tma && nv == pv)
+        return __ldg(reinterpret_cast<const uint4*>(row + static_cast<size_t>(col0) * es));
+    uint32_t wd[4];
+#pragma unroll
+    for (uint32_t i = 0; i < 4; ++i) wd[i] = DT == Q38S_DTYPE_BF16 ? 0xff80ff80u : 0xff800000u;
+    for (uint32_t i = 0; i < nv; ++i) {
+        const uint32_t bits = __float_as_uint(elem_at<DT>(row, col0 + i));
+        if (DT == Q38S_DTYPE_BF16) {
+            const uint32_t h = bits >> 16, sh = 16 * (i & 1);
+            wd[i >> 1] = (wd[i >> 1] & ~(0xffffu << sh)) | (h << sh);
+        } else {
+            wd[i] = bits;
+        }
+    }
+    return make_uint4(wd[0], wd[1], wd[2], wd[3]);
+}
+
+// Whether a unit streams: its row keeps a top-k of at most 256 or a min-p
+// cut (either bounds the candidate set), or the unit is no wider than the
+// candidate buffer; and its tile bounds (2 bytes per thread and tile) leave
+// room for kFinal candidates in the area.  Other units take the general
+// path, which reads the row itself.  The producer and the consumers decide
+// alike (tc: columns per tile).
+__device__ __forceinline__ bool unit_streams(const SampleArgs& a, uint32_t v, uint32_t cols,
+                                             uint32_t tc) {
+    if (((cols + tc - 1) / tc) * kCons * 2u + kFinal * 8u > kArea) return false;
+    const RowParams& p = a.params[state_row(a, v)];
+    const bool minp = a.mode != kModeShardTopK && p.min_p > 0.0f;
+    uint32_t k;
+    if (a.mode == kModeShardTopK) k = a.k_out >= a.vocab ? 0u : a.k_out;
+    else k = (p.top_k == 0 || p.top_k >= a.full_vocab) ? 0u : p.top_k;
+    return minp || (k >= 1 && k <= static_cast<uint32_t>(kCons)) || cols <= kBuf;
 }
 
 // Lower bound of the smallest value v with exp(v - m) >= min_p, for any
@@ -429,25 +454,6 @@ __device__ __forceinline__ bool warp_push(bool push, uint64_t key, uint64_t* buf
     const uint32_t pos = base + __popc(m & ((1u << lane) - 1u));
     if (push && pos < cap) buf[pos] = key;
     return base + __popc(m) > cap;
-}
-
-// Seed threshold from the consumers' keys (one per thread, 0 = none): the
-// largest t on the 2^16 grid with #{keys >= t} >= k, a lower bound of the
-// k-th largest key and hence of the row's k-th largest value (0 when k is 0
-// or above 256 or fewer than k keys exist); *mx gets the largest key.  The
-// search runs bit by bit with every thread voting through a counting
-// barrier.
-__device__ uint32_t seed_select(uint32_t key, uint32_t k, uint32_t* mx, Ctl& c) {
-    *mx = cmax_u32(key, c);
-    uint32_t t = 0;
-    if (k >= 1 && k <= static_cast<uint32_t>(kCons)) {
-#pragma unroll 1
-        for (int b = 31; b >= 16; --b) {
-            const uint32_t cand = t | (1u << b);
-            if (cbar_count(key >= cand) >= k) t = cand;
-        }
-    }
-    return t;
 }
 
 // Exact k-th largest value key (upper 32 bits of the rank keys) among
@@ -588,60 +594,6 @@ __device__ uint32_t finish_buffer(uint64_t* cand, uint32_t n, const Row& r, uint
     if (n > kFinal) return 0xffffffffu;
     sort_desc(cand, n, sorted);
     return r.k_eff ? min(n, r.k_eff) : n;
-}
-
-// ------------------------------------------------------ evaluator buffer
-// The k-th largest value key among buf[0..n) (n >= k >= 1), rounded down to
-// its top 16 bits: the largest t on the 2^16 grid with #{value keys >= t}
-// >= k, found bit by bit with warp sums.  The k-th largest of a subset of
-// the row is at most the row's k-th largest, so it is a valid threshold.
-// One warp.
-__device__ __noinline__ uint32_t buf_kth(const uint64_t* buf, uint32_t n, uint32_t k) {
-    const uint32_t lane = threadIdx.x & 31;
-    uint32_t t = 0;
-    if (n <= 512) {  // value keys in registers, 16 per lane
-        uint32_t e[16];
-#pragma unroll
-        for (int m = 0; m < 16; ++m) {
-            const uint32_t i = lane + 32u * m;
-            e[m] = i < n ? static_cast<uint32_t>(buf[i] >> 32) : 0u;
-        }
-#pragma unroll 1
-        for (int b = 31; b >= 16; --b) {
-            const uint32_t cand = t | (1u << b);
-            uint32_t cnt = 0;
-#pragma unroll
-            for (int m = 0; m < 16; ++m) cnt += e[m] >= cand ? 1u : 0u;
-            if (__reduce_add_sync(0xffffffffu, cnt) >= k) t = cand;
-        }
-        return t;
-    }
-#pragma unroll 1
-    for (int b = 31; b >= 16; --b) {
-        const uint32_t cand = t | (1u << b);
-        uint32_t cnt = 0;
-        for (uint32_t i = lane; i < n; i += 32)
-            cnt += static_cast<uint32_t>(buf[i] >> 32) >= cand ? 1u : 0u;
-        if (__reduce_add_sync(0xffffffffu, cnt) >= k) t = cand;
-    }
-    return t;
-}
-
-// Keeps the entries of buf[0..n) whose value key is >= th, in place (order
-// kept); returns their number.  One warp.
-__device__ __noinline__ uint32_t buf_compact(uint64_t* buf, uint32_t n, uint32_t th) {
-    const uint32_t lane = threadIdx.x & 31;
-    uint32_t out = 0;
-    for (uint32_t i0 = 0; i0 < n; i0 += 32) {
-        const uint32_t i = i0 + lane;
-        const uint64_t e = i < n ? buf[i] : 0ull;
-        const bool keep = i < n && static_cast<uint32_t>(e >> 32) >= th;
-        const uint32_t m = __ballot_sync(0xffffffffu, keep);
-        if (keep) buf[out + __popc(m & ((1u << lane) - 1u))] = e;
-        out += __popc(m);
-    }
-    __syncwarp();
-    return out;
 }
 
 // ---------------------------------------------------------------- epilogue
@@ -1307,10 +1259,8 @@ __device__ void produce(const SampleArgs& a, unsigned char* ring, Ctl& c) {
         const uint32_t v = u / S;
         uint32_t c0, c1;
         chunk_range(a.vocab, S, u % S, c0, c1);
-        const uint32_t srow = state_row(a, v);
-        const bool pen = (a.params[srow].flags & kFlagPenalties) != 0;
+        if (!unit_streams(a, v, c1 - c0, TC)) continue;
         const unsigned char* row = row_ptr<DT>(a, v);
-        const uint32_t* bmrow = a.bitmap + static_cast<size_t>(srow) * a.bitmap_words;
         for (uint32_t t0 = c0; t0 < c1; t0 += TC, ++g) {
             const uint32_t slot = g % kRing;
             if (g >= kRing) {
@@ -1331,239 +1281,13 @@ __device__ void produce(const SampleArgs& a, unsigned char* ring, Ctl& c) {
             const uint32_t n = min(c1 - t0, TC);
             const uint32_t bytes = n * es;
             const uint32_t bulk = a.use_tma ? (bytes & ~15u) : 0u;
-            const uint32_t bmb = pen ? ((n + 127) / 128) * 16 : 0u;
             unsigned char* sl = ring + slot * kSlot;
-            mbar_arrive_expect_tx(&c.full[slot], bulk + bmb);
+            mbar_arrive_expect_tx(&c.full[slot], bulk);
             if (bulk) tma_load_1d(sl, row + static_cast<size_t>(t0) * es, bulk, &c.full[slot]);
-            if (bmb) tma_load_1d(sl + kTileBytes, bmrow + t0 / 32, bmb, &c.full[slot]);
             atomicExch(&c.issued, g + 1);
         }
     }
     atomicExch(&c.prod_done, 1u);
-}
-
-// Evaluator (warp 9): takes the raw candidates the consumers queue, in
-// queue order, 32 per round; gives each its exact value (sampling.cc:76-92)
-// and keeps those at or above theta in the unit's candidate buffer as rank
-// keys.  theta is the best lower bound known of the smallest value the row
-// can keep: the seed's, the k-th largest buffered value and, for min-p
-// rows, M + ln(min_p) - slack with M the largest exact value seen.  Every
-// rise is published to the consumers, whose filter uses it from their next
-// tile on.
-//
-// The k-th largest buffered value is tracked with a 256-bin histogram of
-// value keys laid out from the seed's threshold up to twice the seed's
-// maximum (higher keys count in the top bin): after every round the lower
-// edge of the highest bin at which the count from the top reaches k is a
-// lower bound of the k-th largest buffered value.  Without a seed threshold
-// (top_k above 256) a bit search over the buffer refreshes it instead as
-// the buffer grows.
-//
-// Queue protocol: an entry is 1 << 63 | ((column << 1) | penalised) << 32 |
-// raw value bits; 0 marks a free slot.  A consumer warp reserves up to 32
-// slots at a time on q_head and waits until q_tail leaves room; the
-// evaluator takes the contiguous written prefix, clears it and advances
-// q_tail.  The oldest reservation always has room (it is at most 32 of kQ
-// slots), so every wait ends.
-template <int DT>
-__device__ void evaluate(const SampleArgs& a, unsigned char* area, Ctl& c) {
-    constexpr unsigned kFull = 0xffffffffu;
-    const uint32_t lane = threadIdx.x & 31;
-    uint64_t* buf = reinterpret_cast<uint64_t*>(area);
-    volatile uint64_t* q = reinterpret_cast<volatile uint64_t*>(buf + kBuf);
-    uint32_t* hist = c.hist;
-    const uint32_t S = a.segs;
-    const uint32_t n_units = a.vrows * S;
-    uint32_t tail = 0;     // queue entries taken (all units of this CTA)
-    uint32_t done_at = 0;  // consumer-warp completions that end the unit
-    for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
-        Row r;
-        load_row(a, u / S, r);
-        done_at += kCons / 32;
-        ebar();  // unit start: shared words reset, queue cleared
-#pragma unroll
-        for (int j = 0; j < 8; ++j) hist[lane * 8 + j] = 0;
-        uint32_t theta = 0, pub = 0, mx = 0, n = 0, flags = 0;
-        const uint32_t step = r.k_eff ? max(16u, r.k_eff / 4) : 0u;
-        uint32_t kth_at = r.k_eff ? r.k_eff + step : 0xffffffffu;
-        bool over = false, hist_on = false;
-        uint32_t hbase = 0, hshift = 0;
-        long long idle0 = clock64();
-#ifdef Q38S_TRACE
-        uint32_t tr_entries = 0, tr_rounds = 0, tr_kth = 0;
-        long long tr_kcyc = 0;
-#endif
-        while (true) {
-            const uint64_t e = q[(tail + lane) % kQ];
-            const uint32_t vm = __ballot_sync(kFull, (e >> 63) != 0);
-            const uint32_t run = vm == kFull ? 32u : static_cast<uint32_t>(__ffs(~vm) - 1);
-            if (run == 0) {
-                const uint32_t cd = *reinterpret_cast<volatile uint32_t*>(&c.cons_done);
-                if (static_cast<int32_t>(cd - done_at) >= 0) {
-                    // every consumer warp has queued its last entry
-                    __threadfence_block();
-                    const uint32_t head = *reinterpret_cast<volatile uint32_t*>(&c.q_head);
-                    if (head == tail || *reinterpret_cast<volatile uint32_t*>(&c.abort_flag)) break;
-                }
-                if (clock64() - idle0 > 2 * kWaitLimitCycles) {
-                    flags |= kFTimeout;
-                    if (lane == 0) atomicOr(&c.abort_flag, 1u);
-                    break;
-                }
-                __nanosleep(64);  // leave the issue slots to the consumers
-                continue;
-            }
-            idle0 = clock64();
-#ifdef Q38S_TRACE
-            tr_entries += run;
-            ++tr_rounds;
-#endif
-            // the seed's bounds (published once per unit by the consumers)
-            {
-                const uint32_t ts = *reinterpret_cast<volatile uint32_t*>(&c.theta_pub);
-                const uint32_t ms = *reinterpret_cast<volatile uint32_t*>(&c.mrun);
-                theta = max(theta, ts);
-                if (ms > mx) {
-                    mx = ms;
-                    if (r.minp) theta = max(theta, minp_key(mx, r));
-                }
-                if (!hist_on && r.k_eff && ts >= 0x10000u) {
-                    // bins from the seed threshold up to twice the seed maximum
-                    hist_on = true;
-                    hbase = ts & 0xffff0000u;
-                    const uint32_t range = max(ms, hbase) - hbase;
-                    while ((range >> hshift) >= 128u) ++hshift;
-                }
-            }
-            uint32_t k = 0, tok = 0;
-            bool inf = false;
-            if (lane < run) {
-                q[(tail + lane) % kQ] = 0ull;
-                if (!over) {
-                    const uint32_t col = static_cast<uint32_t>(e >> 33) & 0x3fffffffu;
-                    const bool pen = (e >> 32) & 1u;
-                    tok = a.col_begin + col;
-                    uint64_t count = 1;
-                    if (pen && r.freq)
-                        count = (r.counts_row ? r.counts_row[col] : 0u) + extra_count(r, tok);
-                    const float vx =
-                        transform(__uint_as_float(static_cast<uint32_t>(e)), pen, count, r.p);
-                    inf = vx == INFINITY;
-                    k = float_key(vx);
-                }
-            }
-            tail += run;
-            __syncwarp();
-            if (lane == 0) {
-                __threadfence_block();  // the cleared slots before the new tail
-                *reinterpret_cast<volatile uint32_t*>(&c.q_tail) = tail;
-            }
-            if (over) continue;
-            if (__any_sync(kFull, inf)) flags |= kFInf;
-            const uint32_t bm = __reduce_max_sync(kFull, k);
-            if (bm > mx) {
-                mx = bm;
-                if (r.minp) theta = max(theta, minp_key(mx, r));
-            }
-            bool push = lane < run && k >= theta;
-            if (n + 32 > kBuf && __any_sync(kFull, push)) {
-                // full: compact around the k-th value and theta
-                if (r.k_eff && n > r.k_eff) theta = max(theta, buf_kth(buf, n, r.k_eff));
-                n = buf_compact(buf, n, theta);
-                push = push && k >= theta;
-                if (n + 32 > kBuf) {
-                    // overflow: the row takes the general path; a threshold
-                    // of +inf stops the consumers' queueing
-                    over = true;
-                    flags |= kFOverflow;
-                    if (lane == 0) atomicMax(&c.theta_pub, kPosInfKey);
-                    continue;
-                }
-            }
-            const uint32_t pm = __ballot_sync(kFull, push);
-            if (push) {
-                buf[n + __popc(pm & ((1u << lane) - 1u))] = rank_key(k, tok);
-                if (hist_on) atomicAdd(&hist[min((k - hbase) >> hshift, 255u)], 1u);
-            }
-            n += __popc(pm);
-            if (hist_on) {
-                if (pm) {
-                    __syncwarp();
-                    // highest bin at which the count from the top reaches k
-                    uint32_t h[8], s8 = 0;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        h[j] = hist[255 - 8 * lane - j];
-                        s8 += h[j];
-                    }
-                    uint32_t inc = s8;
-#pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const uint32_t y = __shfl_up_sync(kFull, inc, o);
-                        if (lane >= static_cast<uint32_t>(o)) inc += y;
-                    }
-                    const uint32_t hit = __ballot_sync(kFull, inc >= r.k_eff);
-                    if (hit) {
-                        const uint32_t L = __ffs(hit) - 1;
-                        uint32_t bin = 0;
-                        if (lane == L) {
-                            uint32_t acc = inc - s8;
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) {
-                                acc += h[j];
-                                if (acc >= r.k_eff) {
-                                    bin = 255 - 8 * lane - j;
-                                    break;
-                                }
-                            }
-                        }
-                        bin = __shfl_sync(kFull, bin, L);
-                        theta = max(theta, hbase + (bin << hshift));
-                    }
-                }
-            } else if (n >= kth_at) {
-#ifdef Q38S_TRACE
-                const long long tk0 = clock64();
-                ++tr_kth;
-#endif
-                __syncwarp();
-                theta = max(theta, buf_kth(buf, n, r.k_eff));
-                n = buf_compact(buf, n, theta);
-                kth_at = n + step;
-#ifdef Q38S_TRACE
-                tr_kcyc += clock64() - tk0;
-#endif
-            }
-            if (theta > pub) {
-                pub = theta;
-                if (lane == 0) atomicMax(&c.theta_pub, theta);
-            }
-#ifdef Q38S_TRACE
-            if (g_trace && lane == 0 && u < 256 && tr_rounds <= 32)
-                g_trace[106496 + static_cast<size_t>(u) * 32 + tr_rounds - 1] =
-                    ((gtime() & 0xffffffffull) << 32) | theta;
-#endif
-        }
-        tail = *reinterpret_cast<volatile uint32_t*>(&c.q_head);
-        // drop what the final threshold excludes
-        if (!over && n) n = buf_compact(buf, n, theta);
-#ifdef Q38S_TRACE
-        if (g_trace && lane == 0 && u < 8192) {
-            g_trace[static_cast<size_t>(u) * 16 + 10] = gtime();
-            g_trace[static_cast<size_t>(u) * 16 + 14] =
-                (static_cast<unsigned long long>(tr_entries) << 32) | tr_rounds;
-            g_trace[static_cast<size_t>(u) * 16 + 15] =
-                (static_cast<unsigned long long>(tr_kth) << 32) |
-                static_cast<unsigned long long>(min(tr_kcyc, 0xffffffffll));
-        }
-#endif
-        if (lane == 0) {
-            c.n_cand = over ? 0u : n;
-            if (flags) atomicOr(&c.flags, flags);
-        }
-        __syncwarp();
-        ebar();  // unit end: the consumers finish from the buffer
-    }
 }
 
 template <int DT>
@@ -1590,31 +1314,33 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
         c.prod_done = 0;
         c.issued = 0;
         c.fail_g = 0xffffffffu;
-        c.q_head = 0;
-        c.q_tail = 0;
-        c.cons_done = 0;
         fence_mbar_init();
     }
     __syncthreads();
-    if (tid >= static_cast<uint32_t>(kCons + 32)) {
-        evaluate<DT>(a, area, c);
-        return;
-    }
     if (tid >= static_cast<uint32_t>(kCons)) {
         if (tid == static_cast<uint32_t>(kCons)) produce<DT>(a, ring, c);
         return;
     }
 
-    // Consumers.  Inside a unit the warps run decoupled: each waits for and
-    // releases the slots itself and queues the few elements its filter lets
-    // through for the evaluator warp.  Block barriers: the seed (once per
-    // unit), rare tile fix-ups, and the start and end of the unit.
+    // Consumers.  Per unit:
+    //   stream   every tile of the unit, keeping per thread and tile the
+    //            largest raw value of the thread's four vectors (an upper
+    //            bound, in the area's tail) and the thread's largest raw
+    //            value with its tile;
+    //   theta    the exact values of the 256 threads' largest elements
+    //            (distinct elements) give theta: their k-th largest, and
+    //            for min-p rows M + ln(min_p) - slack with M their largest;
+    //   gather   the thread's tiles whose bound reaches theta's raw bound are
+    //            read again from global memory (L2 holds them: the unit has
+    //            just streamed through) and their elements at or above
+    //            theta join the candidate buffer.
+    // The warps stream decoupled; block barriers come once per unit.
     const uint32_t warp = tid >> 5, lane = tid & 31;
-    uint64_t* qbuf = cand + kBuf;  // the raw-candidate queue
     const uint32_t S = a.segs;
     const uint32_t n_units = a.vrows * S;
     uint32_t g = 0;     // tiles passed (the producer's order)
-    bool stop = false;  // this warp gave up on a copy or a queue slot (warp-uniform)
+    bool stop = false;  // this warp gave up on a copy (warp-uniform)
+    (void)warp;
     for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
         const uint32_t v = u / S, seg = u % S;
         uint32_t c0, c1;
@@ -1624,26 +1350,23 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
         Row r;
         load_row(a, v, r);
         Q38S_TT(u, 1);
+        const bool streams = unit_streams(a, v, c1 - c0, TC);
+        const unsigned char* src_row = row_ptr<DT>(a, v);
+        // per-thread tile bounds in the area's tail; candidates in its head
+        uint16_t* bkey = reinterpret_cast<uint16_t*>(area + kArea) - ntiles * kCons;
+        const uint32_t cap = min(kBuf, (kArea - ntiles * kCons * 2u) / 8u);
         if (tid == 0) {
             c.flags = 0;
-            c.mrun = 0;
-            c.theta_pub = 0;
+            c.n_cand = 0;
 #ifdef Q38S_TRACE
-            c.tr_qwait = 0;
+            c.bc_u32[3] = 0;
 #endif
         }
-        // the queue shares the area with the previous unit's epilogue
-        for (uint32_t i = tid; i < kQ; i += kCons) qbuf[i] = 0ull;
-        ebar();
-        uint32_t theta = 0;
-        uint32_t rho_theta = 1;  // the threshold rho was derived from (1: none yet)
-        float rho = 0.0f;        // raw-logit bound of theta
-        bool hopeless = false;
-        const unsigned char* src_row = row_ptr<DT>(a, v);
-        for (uint32_t t = 0; t < ntiles; ++t, ++g) {
+        float tmax = -INFINITY;  // the thread's largest raw value ...
+        uint32_t tmax_t = 0;     // ... and its tile
+        for (uint32_t t = 0; streams && t < ntiles; ++t, ++g) {
             const uint32_t slot = g % kRing;
             unsigned char* sl = ring + slot * kSlot;
-            uint32_t* sbm = reinterpret_cast<uint32_t*>(sl + kTileBytes);
             const uint32_t t0 = c0 + t * TC;
             const uint32_t n = min(c1 - t0, TC);
 #ifdef Q38S_TRACE
@@ -1662,14 +1385,12 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                 }
             }
             // consumer-side writes into the slot: the part the bulk copy
-            // cannot move (ragged tail, unaligned rows), -inf padding to a
-            // whole vector, this call's additional penalty tokens
+            // cannot move (ragged tail, unaligned rows) and -inf padding to
+            // a whole vector
             const uint32_t bytes = n * es;
             const uint32_t bulk = a.use_tma ? (bytes & ~15u) : 0u;
             const uint32_t padded = ((n + pv - 1) / pv) * pv;
-            const bool fix = bulk < bytes || padded != n;
-            const bool mark = r.pen && r.n_extra > 0;
-            if (fix || mark) {
+            if (bulk < bytes || padded != n) {
                 const bool all_ok = !cbar_or(!ok);
                 if (all_ok) {
                     const unsigned char* src = src_row + static_cast<size_t>(t0) * es;
@@ -1678,243 +1399,234 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                         if (DT == Q38S_DTYPE_BF16) reinterpret_cast<uint16_t*>(sl)[j] = 0xff80u;
                         else reinterpret_cast<uint32_t*>(sl)[j] = 0xff800000u;
                     }
-                    if (mark) {
-                        for (uint32_t e = tid; e < r.n_extra; e += kCons) {
-                            const uint32_t col = static_cast<uint32_t>(r.extra[e]) - a.col_begin;
-                            if (col >= t0 && col < t0 + n)
-                                atomicOr(&sbm[(col - t0) >> 5], 1u << ((col - t0) & 31));
-                        }
-                    }
                 }
                 fence_async_smem();  // generic writes before the slot's next bulk copy
                 cbar();
             }
-            // the thread's vectors of this tile
+            // the largest raw value of the thread's vectors of this tile
             const uint4* vec = reinterpret_cast<const uint4*>(sl);
             const uint32_t nvec = padded / pv;
-            uint4 wv[kU];
-#pragma unroll
-            for (int q = 0; q < kU; ++q) {
-                const uint32_t j = tid + q * kCons;
-                wv[q] = (ok && j < nvec)
-                            ? vec[j]
-                            : (DT == Q38S_DTYPE_BF16
-                                   ? make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u)
-                                   : make_uint4(0xff800000u, 0xff800000u, 0xff800000u,
-                                                0xff800000u));
-            }
-            if (t == 0) {
-#ifdef Q38S_TRACE
-                const long long ts0 = clock64();
-#endif
-                // seed (every warp takes part): a lower bound of the exact
-                // value of each thread's largest raw logit over the tiles
-                // already in the ring (up to four: about a fifth of a row),
-                // then the block's k-th / maximum
-                float best = -INFINITY;
-                int bq = -1;
-#pragma unroll
-                for (int q = 0; q < kU; ++q) {
-                    const float f = vec_max<DT>(wv[q]);
-                    if (f > best) {
-                        best = f;
-                        bq = q;
-                    }
-                }
-                float ahead = -INFINITY;  // the same over the next ring tiles
-                if (ok && !r.freq) {
-#pragma unroll 1
-                    for (uint32_t t2 = 1; t2 < min(ntiles, kRing); ++t2) {
-                        const uint32_t g2 = g + t2;
-                        const uint32_t n2 = min(c1 - (t0 + t2 * TC), TC);
-                        // tiles that need consumer fix-ups are read in their own turn
-                        if (!a.use_tma || (n2 * es) % 16 != 0 || n2 % pv != 0) break;
-                        if (!wait_full(c, g2 % kRing, (g2 / kRing) & 1u)) break;
-                        const uint4* v2 = reinterpret_cast<const uint4*>(ring + (g2 % kRing) * kSlot);
-#pragma unroll
-                        for (int q = 0; q < kU; ++q) {
-                            const uint32_t j = tid + q * kCons;
-                            if (j < n2 / pv) ahead = fmaxf(ahead, vec_max<DT>(v2[j]));
-                        }
-                    }
-                }
-                if (ahead > best) {
-                    best = ahead;
-                    bq = 0;
-                }
-                // Lower bound of the exact value of the thread's largest raw
-                // logit, whatever its penalty bit: the smaller of its
-                // unpenalised and penalised values (no count is needed without
-                // a frequency penalty; those rows find the element instead).
-                uint32_t tk = 0;
-                if (ok && bq >= 0 && !r.freq) {
-                    float lb = exact_value(best, false, 1, r.p);
-                    if (r.pen) lb = fminf(lb, exact_value(best, true, 1, r.p));
-                    tk = float_key(lb);
-                } else if (ok && bq >= 0) {
-                    const uint32_t j = tid + bq * kCons;
-#pragma unroll 1
-                    for (uint32_t e = 0; e < pv; ++e) {
-                        const uint32_t idx = j * pv + e;
-                        if (idx >= n) break;
-                        const float x = load_elem<DT>(sl, idx);
-                        if (x == best) {
-                            const float vx =
-                                eval_slot(r, sbm, x, idx, t0 + idx, a.col_begin + t0 + idx);
-                            if (vx == INFINITY) atomicOr(&c.flags, kFInf);
-                            tk = float_key(vx);
-                            break;
-                        }
-                    }
-                }
-#ifdef Q38S_TRACE
-                const long long ts1 = clock64();
-#endif
-                uint32_t m0;
-                theta = seed_select(tk, r.k_eff, &m0, c);
-#ifdef Q38S_TRACE
-                const long long ts2 = clock64();
-#endif
-                if (r.minp) theta = max(theta, minp_key(m0, r));
-#ifdef Q38S_TRACE
-                const long long ts3 = clock64();
-                if (tid == 0) Q38S_TR(u, 13, ((ts1 - ts0) << 42) | ((ts2 - ts1) << 21) | (ts3 - ts2));
-#endif
-                if (tid == 0) {
-                    atomicMax(&c.mrun, m0);
-                    atomicMax(&c.theta_pub, theta);
-                }
-                hopeless = theta <= kNegInfKey && (c1 - c0) > kBuf;
-                Q38S_TT(u, 2);
-                Q38S_TR(u, 3, (static_cast<unsigned long long>(theta) << 32) | hopeless);
-            } else {
-                // the evaluator's threshold
-                theta = max(theta, *reinterpret_cast<volatile uint32_t*>(&c.theta_pub));
-            }
-            if (ok && !hopeless) {
-                if (theta != rho_theta) {
-                    rho_theta = theta;
-                    const float th = theta <= kNegInfKey ? -INFINITY : key_float(theta);
-                    rho = raw_bound(th, r.p.temperature);
-                }
-                // one packed maximum and compare per 16-byte vector: bit q of
-                // vhit marks a vector that may hold an element at or above rho
-                uint32_t vhit = 0;
+            float bm = -INFINITY;
+            if (ok) {
                 if (DT == Q38S_DTYPE_BF16) {
-                    const __nv_bfloat16 rb = __float2bfloat16_rd(rho);
-                    const __nv_bfloat162 r2 = __halves2bfloat162(rb, rb);
-#pragma unroll
-                    for (int q = 0; q < kU; ++q) {
-                        const __nv_bfloat162 m =
-                            __hmax2(__hmax2(*reinterpret_cast<const __nv_bfloat162*>(&wv[q].x),
-                                            *reinterpret_cast<const __nv_bfloat162*>(&wv[q].y)),
-                                    __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&wv[q].z),
-                                            *reinterpret_cast<const __nv_bfloat162*>(&wv[q].w)));
-                        if (!__hblt2(m, r2)) vhit |= 1u << q;
-                    }
-                } else {
-#pragma unroll
-                    for (int q = 0; q < kU; ++q)
-                        if (!(vec_max<DT>(wv[q]) < rho)) vhit |= 1u << q;
-                }
-                // Elements of those vectors that may reach theta (raw value at
-                // or above rho, or penalised in a row whose penalties can raise
-                // a value): bit q * pv + e of look is element e of vector q.
-                uint32_t look = 0;
-                if (vhit || r.nonmono) {
+                    __nv_bfloat162 m2 = __float2bfloat162_rn(-INFINITY);
 #pragma unroll
                     for (int q = 0; q < kU; ++q) {
                         const uint32_t j = tid + q * kCons;
-                        uint32_t penbits = 0;
-                        if (r.nonmono && j < nvec) {
-                            const uint32_t e0 = j * pv;
-                            penbits = (sbm[e0 >> 5] >> (e0 & 31)) & ((1u << pv) - 1u);
+                        if (j < nvec) {
+                            const uint4 w = vec[j];
+                            m2 = __hmax2(m2, __hmax2(__hmax2(*reinterpret_cast<const __nv_bfloat162*>(&w.x),
+                                                             *reinterpret_cast<const __nv_bfloat162*>(&w.y)),
+                                                     __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&w.z),
+                                                             *reinterpret_cast<const __nv_bfloat162*>(&w.w))));
                         }
-                        if (((vhit >> q) & 1u) || penbits) {
+                    }
+                    bm = fmaxf(__low2float(m2), __high2float(m2));
+                } else {
 #pragma unroll
-                            for (int e = 0; e < static_cast<int>(pv); ++e) {
-                                const float x = vec_elem<DT>(wv[q], e);
-                                if ((!(x < rho) || ((penbits >> e) & 1u)) && j * pv + e < n)
-                                    look |= 1u << (q * pv + e);
-                            }
-                        }
-                    }
-                }
-#ifdef Q38S_TRACE
-                if (g_trace && u < 256 && t < 20) {
-                    const uint32_t nl = __reduce_add_sync(kFull, __popc(look));
-                    if (lane == 0)
-                        g_trace[65536 + (static_cast<size_t>(u) * 20 + t) * 8 + warp] =
-                            (static_cast<unsigned long long>(theta) << 32) | nl;
-                    if (lane == 0 && warp == 0)
-                        g_trace[114688 + static_cast<size_t>(u) * 20 + t] = gtime();
-                }
-#endif
-                // rare path: the looks go to the evaluator's queue as (raw
-                // value, column, penalised bit), at most one per lane and round
-                while (__any_sync(kFull, look != 0)) {
-                    const uint32_t m = __ballot_sync(kFull, look != 0);
-                    uint32_t base = 0, fail = 0;
-                    if (lane == 0) {
-                        const uint32_t need = __popc(m);
-                        base = atomicAdd(&c.q_head, need);
-                        const long long w0 = clock64();
-                        while (base + need - *reinterpret_cast<volatile uint32_t*>(&c.q_tail) > kQ) {
-                            if (*reinterpret_cast<volatile uint32_t*>(&c.abort_flag) ||
-                                clock64() - w0 > kWaitLimitCycles) {
-                                fail = 1;
-                                break;
-                            }
-                        }
-#ifdef Q38S_TRACE
-                        atomicAdd(&c.tr_qwait, static_cast<unsigned long long>(clock64() - w0));
-#endif
-                        __threadfence_block();  // the evaluator's clears before our entries
-                    }
-                    base = __shfl_sync(kFull, base, 0);
-                    if (__shfl_sync(kFull, fail, 0)) {
-                        stop = true;
-                        if (lane == 0) atomicOr(&c.abort_flag, 1u);
-                        break;
-                    }
-                    if (look) {
-                        const uint32_t b = __ffs(look) - 1;
-                        look &= look - 1;
-                        const uint32_t idx = (tid + (b / pv) * kCons) * pv + (b % pv);
-                        const uint32_t pen = r.pen ? (sbm[idx >> 5] >> (idx & 31)) & 1u : 0u;
-                        const float x = load_elem<DT>(sl, idx);
-                        reinterpret_cast<volatile uint64_t*>(qbuf)[(base + __popc(m & ((1u << lane) - 1u))) % kQ] =
-                            (1ull << 63) |
-                            (static_cast<uint64_t>(((t0 + idx) << 1) | pen) << 32) |
-                            __float_as_uint(x);
+                    for (int q = 0; q < kU; ++q) {
+                        const uint32_t j = tid + q * kCons;
+                        if (j < nvec) bm = fmaxf(bm, vec_max<DT>(vec[j]));
                     }
                 }
             }
-            __syncwarp();
-            // release the slot once every lane has read it; a slot whose
-            // wait failed is never released (its copy may still land)
+            // bf16 rounded up: an upper bound of every element of the block
+            bkey[t * kCons + tid] = __bfloat16_as_ushort(__float2bfloat16_ru(bm));
+            if (bm > tmax) {
+                tmax = bm;
+                tmax_t = t;
+            }
 #ifdef Q38S_TRACE
             if (g_trace && u < 256 && t < 20 && lane == 0 && warp == 0)
                 g_trace[119808 + static_cast<size_t>(u) * 20 + t] =
                     (static_cast<unsigned long long>(tw1 - tw0) << 32) |
                     static_cast<unsigned long long>(clock64() - tw1);
 #endif
+            // release the slot once every lane has read it; a slot whose
+            // wait failed is never released (its copy may still land)
+            __syncwarp();
             if (ok && lane == 0) mbar_arrive(&c.empty[slot]);
         }
-        // ---- end of unit: every queued entry is written; the evaluator
-        // drains the queue and leaves the candidates in cand[0..n)
-        __syncwarp();
-        if (lane == 0) {
-            __threadfence_block();
-            atomicAdd(&c.cons_done, 1u);
-        }
         const bool any_stop = cbar_or(stop);
-        ebar();
+        Q38S_TT(u, 2);
+        uint32_t theta = 0;
+        bool overflow = !streams;
+        if (streams && !any_stop) {
+            // ---- theta: the exact value of the thread's largest element
+            // (found again among its vectors of tile tmax_t; distinct
+            // elements per thread keep theta a lower bound), then the k-th
+            // largest and the largest of the 256 keys (warp 0)
+            uint32_t tk = 0;
+            if (tmax > -INFINITY) {
+                const uint32_t t0 = c0 + tmax_t * TC;
+                const uint32_t n = min(c1 - t0, TC);
+                uint32_t col = 0xffffffffu, pwc = 0;
+                float x = 0.0f;
+                uint4 w[kU];
+                uint32_t pw[kU];
+#pragma unroll
+                for (int q = 0; q < kU; ++q) {  // every load in flight at once
+                    const uint32_t e0 = (tid + q * kCons) * pv;
+                    const uint32_t nv = e0 < n ? min(pv, n - e0) : 0u;
+                    w[q] = nv ? load_vec<DT>(a, src_row, t0 + e0, nv)
+                              : make_uint4(0u, 0u, 0u, 0u);
+                    pw[q] = (nv && r.pen) ? __ldg(&r.gbm[(t0 + e0) >> 5]) : 0u;
+                }
+#pragma unroll
+                for (int q = 0; q < kU; ++q) {
+                    const uint32_t e0 = (tid + q * kCons) * pv;
+#pragma unroll
+                    for (uint32_t e = 0; e < pv; ++e) {
+                        const float xe = vec_elem<DT>(w[q], static_cast<int>(e));
+                        if (col == 0xffffffffu && e0 + e < n && xe == tmax) {
+                            col = t0 + e0 + e;
+                            x = xe;
+                            pwc = pw[q];
+                        }
+                    }
+                }
+                if (col != 0xffffffffu) {
+                    const float vx = exact_pw(a, r, x, col, pwc);
+                    if (vx == INFINITY) atomicOr(&c.flags, kFInf);
+                    tk = float_key(vx);
+                }
+            }
+            c.tkey[tid] = tk;
+            cbar();
+            if (warp == 0) {
+                uint32_t kk[kCons / 32], mx = 0;
+#pragma unroll
+                for (int i = 0; i < kCons / 32; ++i) {
+                    kk[i] = c.tkey[lane + 32 * i];
+                    mx = max(mx, kk[i]);
+                }
+                mx = __reduce_max_sync(kFull, mx);
+                uint32_t tt = 0;
+                if (r.k_eff >= 1 && r.k_eff <= static_cast<uint32_t>(kCons)) {
+#pragma unroll 1
+                    for (int b = 31; b >= 16; --b) {
+                        const uint32_t cand = tt | (1u << b);
+                        uint32_t cnt = 0;
+#pragma unroll
+                        for (int i = 0; i < kCons / 32; ++i) cnt += kk[i] >= cand ? 1u : 0u;
+                        if (__reduce_add_sync(kFull, cnt) >= r.k_eff) tt = cand;
+                    }
+                }
+                if (lane == 0) {
+                    c.bc_u32[0] = tt;
+                    c.bc_u32[1] = mx;
+                }
+            }
+            cbar();
+            theta = c.bc_u32[0];
+            const uint32_t m0 = c.bc_u32[1];
+            if (r.minp) theta = max(theta, minp_key(m0, r));
+            Q38S_TR(u, 3, theta);
+            Q38S_TT(u, 6);
+            overflow = theta <= kNegInfKey && (c1 - c0) > cap;
+        }
+        if (streams && !any_stop && !overflow) {
+            // ---- gather: every element whose exact value may reach theta
+            const float rho = raw_bound(theta <= kNegInfKey ? -INFINITY : key_float(theta),
+                                        r.p.temperature);
+            auto consider = [&](float x, uint32_t col, uint32_t pw) {
+                const float vx = exact_pw(a, r, x, col, pw);
+                const uint32_t k = float_key(vx);
+                if (vx == INFINITY) atomicOr(&c.flags, kFInf);
+                if (k >= theta) {
+                    const uint32_t at = atomicAdd(&c.n_cand, 1u);
+                    if (at < cap) cand[at] = rank_key(k, a.col_begin + col);
+                }
+            };
+            // the thread's tiles whose bound reaches rho (a NaN bound counts)
+            uint64_t hm = 0;
+#pragma unroll 4
+            for (uint32_t t = 0; t < ntiles; ++t) {
+                const float bound = __bfloat162float(__ushort_as_bfloat16(bkey[t * kCons + tid]));
+                if (!(bound < rho)) hm |= 1ull << t;
+            }
+#ifdef Q38S_TRACE
+            atomicAdd(&c.bc_u32[3], __popcll(hm));
+            Q38S_TT(u, 10);
+#endif
+            while (hm) {
+                const uint32_t t = __ffsll(static_cast<long long>(hm)) - 1;
+                hm &= hm - 1;
+                const uint32_t t0 = c0 + t * TC;
+                const uint32_t n = min(c1 - t0, TC);
+                uint4 w[kU];
+                uint32_t pw[kU];
+#pragma unroll
+                for (int q = 0; q < kU; ++q) {  // every load in flight at once
+                    const uint32_t e0 = (tid + q * kCons) * pv;
+                    const uint32_t nv = e0 < n ? min(pv, n - e0) : 0u;
+                    w[q] = nv ? load_vec<DT>(a, src_row, t0 + e0, nv)
+                              : make_uint4(0u, 0u, 0u, 0u);
+                    pw[q] = (nv && r.pen) ? __ldg(&r.gbm[(t0 + e0) >> 5]) : 0u;
+                }
+                uint32_t cm = 0;  // bit q * pv + e: element e of vector q reaches rho
+#pragma unroll
+                for (int q = 0; q < kU; ++q) {
+                    const uint32_t e0 = (tid + q * kCons) * pv;
+#pragma unroll
+                    for (uint32_t e = 0; e < pv; ++e) {
+                        const float x = vec_elem<DT>(w[q], static_cast<int>(e));
+                        if (e0 + e < n && !(x < rho)) cm |= 1u << (q * pv + e);
+                    }
+                }
+                while (cm) {
+                    const uint32_t b = __ffs(cm) - 1;
+                    cm &= cm - 1;
+                    const uint32_t qv = b / pv, ev = b % pv;
+                    uint4 wq = w[0];
+                    uint32_t pq = pw[0];
+#pragma unroll
+                    for (int q = 1; q < kU; ++q)
+                        if (qv == static_cast<uint32_t>(q)) {
+                            wq = w[q];
+                            pq = pw[q];
+                        }
+                    float x = 0.0f;
+#pragma unroll
+                    for (uint32_t e = 0; e < pv; ++e)
+                        if (ev == e) x = vec_elem<DT>(wq, static_cast<int>(e));
+                    consider(x, t0 + (tid + qv * kCons) * pv + ev, pq);
+                }
+            }
+            if (r.nonmono) {
+                // penalties can raise a value: every penalised element below
+                // rho as well (the state row's bitmap, then this call's
+                // additional tokens that the bitmap does not hold, once each)
+                for (uint32_t wd = c0 / 32 + tid; wd * 32 < c1; wd += kCons) {
+                    uint32_t bits = r.gbm[wd];
+                    while (bits) {
+                        const uint32_t col = wd * 32 + __ffs(bits) - 1;
+                        bits &= bits - 1;
+                        if (col < c0 || col >= c1) continue;
+                        const float x = elem_at<DT>(src_row, col);
+                        if (x < rho) consider(x, col, r.gbm[wd]);
+                    }
+                }
+                for (uint32_t e = tid; e < r.n_extra; e += kCons) {
+                    const uint32_t col = static_cast<uint32_t>(r.extra[e]) - a.col_begin;
+                    if (col < c0 || col >= c1) continue;
+                    if ((r.gbm[col >> 5] >> (col & 31)) & 1u) continue;
+                    bool first = true;
+                    for (uint32_t e2 = 0; e2 < e && first; ++e2) first = r.extra[e2] != r.extra[e];
+                    if (!first) continue;
+                    const float x = elem_at<DT>(src_row, col);
+                    if (x < rho) consider(x, col, 0u);
+                }
+            }
+        }
+        cbar();
+        Q38S_TR(u, 14, c.bc_u32[3]);
         uint32_t flags = c.flags;
-        const uint32_t n = c.n_cand;
-        Q38S_TR(u, 6, c.tr_qwait);
+        uint32_t n = c.n_cand;
+        if (n > cap) overflow = true;
+        if (overflow) n = 0;
         if (any_stop) flags |= kFTimeout;
-        if (hopeless) flags |= kFOverflow;
+        if (overflow) flags |= kFOverflow;
         if (a.mode == kModeShardTopK) flags &= ~kFInf;
         Q38S_TT(u, 4);
         Q38S_TR(u, 5, (static_cast<unsigned long long>(flags) << 32) | n);
