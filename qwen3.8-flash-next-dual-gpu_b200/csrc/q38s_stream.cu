@@ -1447,64 +1447,76 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(&c.empty[slot]);
         }
-        const bool any_stop = cbar_or(stop);
+        // ---- the exact value of the thread's largest element (found again
+        // among its vectors of tile tmax_t; one element per thread keeps the
+        // k-th largest key a lower bound of the row's), before the barrier
+        // so that its loads overlap the other warps' last tiles
+        uint32_t tk = 0;
+        if (streams && !stop && tmax > -INFINITY) {
+            const uint32_t t0 = c0 + tmax_t * TC;
+            const uint32_t n = min(c1 - t0, TC);
+            uint32_t col = 0xffffffffu, pwc = 0;
+            float x = 0.0f;
+            uint4 w[kU];
+            uint32_t pw[kU];
+#pragma unroll
+            for (int q = 0; q < kU; ++q) {  // every load in flight at once
+                const uint32_t e0 = (tid + q * kCons) * pv;
+                const uint32_t nv = e0 < n ? min(pv, n - e0) : 0u;
+                w[q] = nv ? load_vec<DT>(a, src_row, t0 + e0, nv)
+                          : make_uint4(0u, 0u, 0u, 0u);
+                pw[q] = (nv && r.pen) ? __ldg(&r.gbm[(t0 + e0) >> 5]) : 0u;
+            }
+#pragma unroll
+            for (int q = 0; q < kU; ++q) {
+                const uint32_t e0 = (tid + q * kCons) * pv;
+#pragma unroll
+                for (uint32_t e = 0; e < pv; ++e) {
+                    const float xe = vec_elem<DT>(w[q], static_cast<int>(e));
+                    if (col == 0xffffffffu && e0 + e < n && xe == tmax) {
+                        col = t0 + e0 + e;
+                        x = xe;
+                        pwc = pw[q];
+                    }
+                }
+            }
+            if (col != 0xffffffffu) {
+                const float vx = exact_pw(a, r, x, col, pwc);
+                if (vx == INFINITY) atomicOr(&c.flags, kFInf);
+                tk = float_key(vx);
+            }
+        }
+        c.tkey[tid] = tk;
+        const bool any_stop = cbar_or(stop);  // also publishes the keys
         Q38S_TT(u, 2);
         uint32_t theta = 0;
         bool overflow = !streams;
         if (streams && !any_stop) {
-            // ---- theta: the exact value of the thread's largest element
-            // (found again among its vectors of tile tmax_t; distinct
-            // elements per thread keep theta a lower bound), then the k-th
-            // largest and the largest of the 256 keys (warp 0)
-            uint32_t tk = 0;
-            if (tmax > -INFINITY) {
-                const uint32_t t0 = c0 + tmax_t * TC;
-                const uint32_t n = min(c1 - t0, TC);
-                uint32_t col = 0xffffffffu, pwc = 0;
-                float x = 0.0f;
-                uint4 w[kU];
-                uint32_t pw[kU];
-#pragma unroll
-                for (int q = 0; q < kU; ++q) {  // every load in flight at once
-                    const uint32_t e0 = (tid + q * kCons) * pv;
-                    const uint32_t nv = e0 < n ? min(pv, n - e0) : 0u;
-                    w[q] = nv ? load_vec<DT>(a, src_row, t0 + e0, nv)
-                              : make_uint4(0u, 0u, 0u, 0u);
-                    pw[q] = (nv && r.pen) ? __ldg(&r.gbm[(t0 + e0) >> 5]) : 0u;
-                }
-#pragma unroll
-                for (int q = 0; q < kU; ++q) {
-                    const uint32_t e0 = (tid + q * kCons) * pv;
-#pragma unroll
-                    for (uint32_t e = 0; e < pv; ++e) {
-                        const float xe = vec_elem<DT>(w[q], static_cast<int>(e));
-                        if (col == 0xffffffffu && e0 + e < n && xe == tmax) {
-                            col = t0 + e0 + e;
-                            x = xe;
-                            pwc = pw[q];
-                        }
-                    }
-                }
-                if (col != 0xffffffffu) {
-                    const float vx = exact_pw(a, r, x, col, pwc);
-                    if (vx == INFINITY) atomicOr(&c.flags, kFInf);
-                    tk = float_key(vx);
-                }
-            }
-            c.tkey[tid] = tk;
-            cbar();
+            // ---- theta: the k-th largest and the largest of the 256 keys
+            // (warp 0)
             if (warp == 0) {
-                uint32_t kk[kCons / 32], mx = 0;
+                uint32_t kk[kCons / 32], mx = 0, mn = 0xffffffffu, nz = 0;
 #pragma unroll
                 for (int i = 0; i < kCons / 32; ++i) {
                     kk[i] = c.tkey[lane + 32 * i];
                     mx = max(mx, kk[i]);
+                    if (kk[i]) {
+                        mn = min(mn, kk[i]);
+                        ++nz;
+                    }
                 }
                 mx = __reduce_max_sync(kFull, mx);
+                mn = __reduce_min_sync(kFull, mn);
+                nz = __reduce_add_sync(kFull, nz);
                 uint32_t tt = 0;
-                if (r.k_eff >= 1 && r.k_eff <= static_cast<uint32_t>(kCons)) {
+                if (r.k_eff >= 1 && r.k_eff <= nz) {
+                    // the k-th largest key lies in [mn, mx]: the bits above
+                    // the highest one where those differ are fixed
+                    const uint32_t diff = (mx ^ mn) & 0xffff0000u;
+                    const int top = diff ? 31 - __clz(diff) : 15;
+                    tt = top == 31 ? 0u : (mx & ~((2u << top) - 1u)) & 0xffff0000u;
 #pragma unroll 1
-                    for (int b = 31; b >= 16; --b) {
+                    for (int b = top; b >= 16; --b) {
                         const uint32_t cand = tt | (1u << b);
                         uint32_t cnt = 0;
 #pragma unroll
@@ -1549,16 +1561,28 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             atomicAdd(&c.bc_u32[3], __popcll(hm));
             Q38S_TT(u, 10);
 #endif
+            // one list of (tile, thread) blocks for the whole CTA, so that no
+            // thread reads more than its share (the bounds' space is free
+            // once every thread has read its own)
+            uint32_t n_hit;
+            uint32_t hoff = cscan_excl(__popcll(hm), &n_hit, c);
+            uint16_t* hlist = bkey;
             while (hm) {
                 const uint32_t t = __ffsll(static_cast<long long>(hm)) - 1;
                 hm &= hm - 1;
+                hlist[hoff++] = static_cast<uint16_t>(t * kCons + tid);
+            }
+            cbar();
+#pragma unroll 1
+            for (uint32_t hi = tid; hi < n_hit; hi += kCons) {
+                const uint32_t t = hlist[hi] / kCons, thr = hlist[hi] % kCons;
                 const uint32_t t0 = c0 + t * TC;
                 const uint32_t n = min(c1 - t0, TC);
                 uint4 w[kU];
                 uint32_t pw[kU];
 #pragma unroll
                 for (int q = 0; q < kU; ++q) {  // every load in flight at once
-                    const uint32_t e0 = (tid + q * kCons) * pv;
+                    const uint32_t e0 = (thr + q * kCons) * pv;
                     const uint32_t nv = e0 < n ? min(pv, n - e0) : 0u;
                     w[q] = nv ? load_vec<DT>(a, src_row, t0 + e0, nv)
                               : make_uint4(0u, 0u, 0u, 0u);
@@ -1567,7 +1591,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                 uint32_t cm = 0;  // bit q * pv + e: element e of vector q reaches rho
 #pragma unroll
                 for (int q = 0; q < kU; ++q) {
-                    const uint32_t e0 = (tid + q * kCons) * pv;
+                    const uint32_t e0 = (thr + q * kCons) * pv;
 #pragma unroll
                     for (uint32_t e = 0; e < pv; ++e) {
                         const float x = vec_elem<DT>(w[q], static_cast<int>(e));
@@ -1590,7 +1614,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
 #pragma unroll
                     for (uint32_t e = 0; e < pv; ++e)
                         if (ev == e) x = vec_elem<DT>(wq, static_cast<int>(e));
-                    consider(x, t0 + (tid + qv * kCons) * pv + ev, pq);
+                    consider(x, t0 + (thr + qv * kCons) * pv + ev, pq);
                 }
             }
             if (r.nonmono) {
