@@ -540,9 +540,10 @@ __device__ void sort_desc(const uint64_t* keys, uint32_t n, uint64_t* out) {
 
 // Exact top-k / min-p cuts of the candidate buffer, then the sorted prefix
 // into `sorted`.  Returns the number kept, or ~0u when more than kFinal
-// candidates survive the cuts.
+// candidates survive the cuts.  A row's final list (final_list) of at most
+// 256 candidates skips the min-p cut here: the epilogue makes the same cut.
 __device__ uint32_t finish_buffer(uint64_t* cand, uint32_t n, const Row& r, uint64_t* sorted,
-                                  Ctl& c) {
+                                  Ctl& c, bool final_list) {
     if (n <= static_cast<uint32_t>(kCons)) {
         // exact sort by rank counting (rank keys are distinct), then the
         // top-k and min-p cuts are prefix lengths
@@ -554,7 +555,8 @@ __device__ uint32_t finish_buffer(uint64_t* cand, uint32_t n, const Row& r, uint
         }
         cbar();
         uint32_t keep = r.k_eff ? min(n, r.k_eff) : n;
-        if (r.minp && keep) {
+        // a row's final list gets its min-p cut in the epilogue
+        if (r.minp && keep && !final_list) {
             const float M = rank_value(sorted[0]);
             if (isfinite(M)) {
                 const double floor_w = static_cast<double>(r.p.min_p);
@@ -633,8 +635,21 @@ __device__ void epilogue(const uint64_t* sorted, uint32_t n, const RowParams& p,
                 n = m;
             }
             if (lane == 0) {
+                // sequential sum (the reference's order); loads in batches of
+                // 8 so that only the additions are serial
                 double acc = 0.0;
-                for (uint32_t i = 0; i < n; ++i) {
+                uint32_t i = 0;
+                for (; i + 8 <= n; i += 8) {
+                    double v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[j] = w[i + j];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        acc += v[j];
+                        S[i + j] = acc;
+                    }
+                }
+                for (; i < n; ++i) {
                     acc += w[i];
                     S[i] = acc;
                 }
@@ -652,10 +667,20 @@ __device__ void epilogue(const uint64_t* sorted, uint32_t n, const RowParams& p,
                     if (lane == 0) {
                         const double top_p = static_cast<double>(p.top_p);
                         double cum = 0.0;
-                        while (k < n) {
-                            cum += q[k];
-                            ++k;
-                            if (cum >= top_p) break;
+                        bool hit = false;
+                        while (k < n && !hit) {
+                            // the reference's loop, with loads in batches of 8
+                            double v[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) v[j] = k + j < n ? q[k + j] : 0.0;
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                if (!hit && k < n) {
+                                    cum += v[j];
+                                    ++k;
+                                    if (cum >= top_p) hit = true;
+                                }
+                            }
                         }
                     }
                     r = __shfl_sync(kFull, k, 0);
@@ -1656,7 +1681,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
         Q38S_TR(u, 5, (static_cast<unsigned long long>(flags) << 32) | n);
         uint32_t keep = 0;
         if (!(flags & (kFTimeout | kFInf | kFOverflow))) {
-            keep = finish_buffer(cand, n, r, sorted, c);
+            keep = finish_buffer(cand, n, r, sorted, c, S == 1);
             if (keep == 0xffffffffu) flags |= kFOverflow;
         }
         Q38S_TT(u, 7);
@@ -1717,7 +1742,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                         cand[off2 + i] = __ldcg(reinterpret_cast<const unsigned long long*>(src + i));
                 }
                 cbar();
-                rkeep = finish_buffer(cand, rtotal, r, sorted, c);
+                rkeep = finish_buffer(cand, rtotal, r, sorted, c, true);
                 if (rkeep == 0xffffffffu) rflags |= kFOverflow;
             }
             if (tid == 0) a.row_ticket[v] = 0;  // every segment has arrived: reset for the next call
