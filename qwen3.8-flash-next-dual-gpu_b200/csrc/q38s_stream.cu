@@ -155,15 +155,6 @@ __device__ uint32_t cmin_u32(uint32_t v, Ctl& c) {
     for (int i = 1; i < kCons / 32; ++i) r = min(r, c.red_u32[i]);
     return r;
 }
-__device__ uint32_t cor_u32(uint32_t v, Ctl& c) {
-    for (int o = 16; o > 0; o >>= 1) v |= __shfl_xor_sync(0xffffffffu, v, o);
-    cbar();
-    if ((threadIdx.x & 31) == 0) c.red_u32[threadIdx.x >> 5] = v;
-    cbar();
-    uint32_t r = 0;
-    for (int i = 0; i < kCons / 32; ++i) r |= c.red_u32[i];
-    return r;
-}
 __device__ uint32_t csum_u32(uint32_t v, Ctl& c) {
     v = warp_sum_u32(v);
     cbar();
@@ -1713,37 +1704,78 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                 continue;
             }
             __threadfence();
-            // segment headers in parallel (thread s reads segment s), then
-            // every segment's list lands at its prefix offset in cand
-            uint32_t my_len = 0, my_flags = 0;
+            // Segment headers in parallel (thread s reads segment s's length,
+            // flags, largest entry and k-th entry).  The lists are sorted, so
+            // the row's k-th largest value is at least every segment's k-th,
+            // and the row's largest value is the largest first entry: only
+            // entries at or above the better of that bound and the min-p
+            // bound need to be merged.
+            uint32_t my_len = 0, my_flags = 0, my_kth = 0, my_top = 0;
             if (tid < S) {
+                const uint64_t* src = a.seg_keys + static_cast<size_t>(v * S + tid) * kSegCap;
                 my_len = __ldcg(&a.seg_hdr[(v * S + tid) * 4 + 0]);
                 my_flags = __ldcg(&a.seg_hdr[(v * S + tid) * 4 + 1]);
+                const uint64_t top = __ldcg(reinterpret_cast<const unsigned long long*>(src));
+                const uint64_t kth = (r.k_eff && r.k_eff <= kSegCap)
+                    ? __ldcg(reinterpret_cast<const unsigned long long*>(src + r.k_eff - 1)) : 0ull;
+                if (my_len) my_top = static_cast<uint32_t>(top >> 32);
+                if (r.k_eff && my_len >= r.k_eff) my_kth = static_cast<uint32_t>(kth >> 32);
             }
+            if (tid == 0) c.n_cand = 0;
             uint32_t rtotal;
             const uint32_t rel_off = cscan_excl(my_len, &rtotal, c);
-            uint32_t rflags = cor_u32(my_flags, c);
+            if (tid < S) {
+                c.hist[tid] = rel_off;
+                c.hist[64 + tid] = my_flags;
+                c.hist[128 + tid] = my_kth;
+                c.hist[192 + tid] = my_top;
+            }
+            cbar();
+            uint32_t rflags = 0, mkth = 0, mtop = 0;
+#pragma unroll 4
+            for (uint32_t s2 = 0; s2 < S; ++s2) {
+                rflags |= c.hist[64 + s2];
+                mkth = max(mkth, c.hist[128 + s2]);
+                mtop = max(mtop, c.hist[192 + s2]);
+            }
             if (a.mode == kModeShardTopK) rflags &= ~kFInf;
             uint32_t rkeep = 0;
-            if (!(rflags & (kFTimeout | kFInf | kFOverflow)) && rtotal > kBuf) rflags |= kFOverflow;
             if (!(rflags & (kFTimeout | kFInf | kFOverflow))) {
-                cbar();
-                if (tid < S) {
-                    c.hist[tid] = my_len;
-                    c.hist[128 + tid] = rel_off;
+                uint32_t th = mkth;
+                if (r.minp) th = max(th, minp_key(mtop, r));
+                // every entry (flattened over the segments, a handful per
+                // thread, all loads in flight at once) at or above th
+                constexpr int kPer = kBuf / kCons;
+                uint64_t e[kPer];
+#pragma unroll
+                for (int j = 0; j < kPer; ++j) {
+                    const uint32_t idx = tid + j * kCons;
+                    e[j] = 0ull;
+                    if (idx < rtotal && idx < kBuf) {
+                        uint32_t lo = 0, hi = S - 1;  // last segment starting at or before idx
+                        while (lo < hi) {
+                            const uint32_t mid = (lo + hi + 1) / 2;
+                            if (c.hist[mid] <= idx) lo = mid;
+                            else hi = mid - 1;
+                        }
+                        e[j] = __ldcg(reinterpret_cast<const unsigned long long*>(
+                            a.seg_keys + static_cast<size_t>(v * S + lo) * kSegCap + (idx - c.hist[lo])));
+                    }
                 }
-                cbar();
-                // warp w copies segments w, w + 8, ... with lane-strided loads
-                for (uint32_t s2 = warp; s2 < S; s2 += kCons / 32) {
-                    const uint32_t len2 = c.hist[s2];
-                    const uint32_t off2 = c.hist[128 + s2];
-                    const uint64_t* src = a.seg_keys + static_cast<size_t>(v * S + s2) * kSegCap;
-                    for (uint32_t i = lane; i < len2; i += 32)
-                        cand[off2 + i] = __ldcg(reinterpret_cast<const unsigned long long*>(src + i));
+                bool over = rtotal > kBuf;
+#pragma unroll
+                for (int j = 0; j < kPer; ++j) {
+                    const uint32_t idx = tid + j * kCons;
+                    const bool keep = idx < rtotal && idx < kBuf && static_cast<uint32_t>(e[j] >> 32) >= th;
+                    over |= warp_push(keep, e[j], cand, kBuf, &c.n_cand);
                 }
-                cbar();
-                rkeep = finish_buffer(cand, rtotal, r, sorted, c, true);
-                if (rkeep == 0xffffffffu) rflags |= kFOverflow;
+                over = cbar_or(over);
+                const uint32_t nm = min(c.n_cand, kBuf);
+                if (over) rflags |= kFOverflow;  // more than the buffer holds
+                if (!(rflags & kFOverflow)) {
+                    rkeep = finish_buffer(cand, nm, r, sorted, c, true);
+                    if (rkeep == 0xffffffffu) rflags |= kFOverflow;
+                }
             }
             if (tid == 0) a.row_ticket[v] = 0;  // every segment has arrived: reset for the next call
             Q38S_TR(u, 8, 4 + ((rflags & kFOverflow) ? 1 : 0));
