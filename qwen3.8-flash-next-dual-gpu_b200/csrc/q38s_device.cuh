@@ -133,6 +133,12 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
         "l"(src), "r"(bytes), "r"(smem_addr(bar))
         : "memory");
 }
+// atomicAdd with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
     uint32_t ok;
     asm volatile(

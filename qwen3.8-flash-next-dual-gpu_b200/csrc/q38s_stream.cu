@@ -1694,43 +1694,48 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                 a.seg_hdr[u * 4 + 0] = len;
                 a.seg_hdr[u * 4 + 1] = flags;
             }
-            __threadfence();
             cbar();
-            if (tid == 0) c.bc_u32[2] = atomicAdd(&a.row_ticket[v], 1u) == S - 1;
+            // one GPU-scope acquire-release ticket: it publishes the CTA's
+            // writes above (ordered before it by the barrier) and, for the
+            // last segment, makes every other segment's writes visible
+            if (tid == 0) c.bc_u32[2] = atom_add_acq_rel_gpu(&a.row_ticket[v], 1u) == S - 1;
             cbar();
             if (!c.bc_u32[2]) {
                 Q38S_TR(u, 8, 3);
                 Q38S_TT(u, 9);
                 continue;
             }
-            __threadfence();
             // Segment headers in parallel (thread s reads segment s's length,
             // flags, largest entry and k-th entry).  The lists are sorted, so
             // the row's k-th largest value is at least every segment's k-th,
             // and the row's largest value is the largest first entry: only
             // entries at or above the better of that bound and the min-p
             // bound need to be merged.
-            uint32_t my_len = 0, my_flags = 0, my_kth = 0, my_top = 0;
+            uint32_t my_len = 0, my_flags = 0, my_kth = 0, my_top = 0, my_2nd = 0;
+            uint64_t top64 = 0, snd64 = 0;  // the segment's first two entries
             if (tid < S) {
                 const uint64_t* src = a.seg_keys + static_cast<size_t>(v * S + tid) * kSegCap;
                 my_len = __ldcg(&a.seg_hdr[(v * S + tid) * 4 + 0]);
                 my_flags = __ldcg(&a.seg_hdr[(v * S + tid) * 4 + 1]);
                 const uint64_t top = __ldcg(reinterpret_cast<const unsigned long long*>(src));
+                const uint64_t snd = __ldcg(reinterpret_cast<const unsigned long long*>(src + 1));
                 const uint64_t kth = (r.k_eff && r.k_eff <= kSegCap)
                     ? __ldcg(reinterpret_cast<const unsigned long long*>(src + r.k_eff - 1)) : 0ull;
                 if (my_len) my_top = static_cast<uint32_t>(top >> 32);
+                if (my_len > 1) my_2nd = static_cast<uint32_t>(snd >> 32);
+                top64 = top;
+                snd64 = snd;
                 if (r.k_eff && my_len >= r.k_eff) my_kth = static_cast<uint32_t>(kth >> 32);
             }
             if (tid == 0) c.n_cand = 0;
-            uint32_t rtotal;
-            const uint32_t rel_off = cscan_excl(my_len, &rtotal, c);
+            Q38S_TT(u, 13);
             if (tid < S) {
-                c.hist[tid] = rel_off;
                 c.hist[64 + tid] = my_flags;
                 c.hist[128 + tid] = my_kth;
                 c.hist[192 + tid] = my_top;
             }
             cbar();
+            Q38S_TT(u, 15);
             uint32_t rflags = 0, mkth = 0, mtop = 0;
 #pragma unroll 4
             for (uint32_t s2 = 0; s2 < S; ++s2) {
@@ -1738,44 +1743,91 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                 mkth = max(mkth, c.hist[128 + s2]);
                 mtop = max(mtop, c.hist[192 + s2]);
             }
+            // the k-th largest of the segments' two first entries (distinct
+            // entries of the union) bounds the row's k-th largest too
+            if (r.k_eff && r.k_eff <= 2 * S) {
+                cbar();
+                if (tid < S) {
+                    c.tkey[2 * tid] = my_top;
+                    c.tkey[2 * tid + 1] = my_2nd;
+                }
+                cbar();
+                if (warp == 0) {
+                    uint32_t kk[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint32_t j = lane + 32u * i;
+                        kk[i] = j < 2 * S ? c.tkey[j] : 0u;
+                    }
+                    uint32_t tt = 0;
+#pragma unroll 1
+                    for (int b = 31; b >= 16; --b) {
+                        const uint32_t cand = tt | (1u << b);
+                        uint32_t cnt = 0;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) cnt += kk[i] >= cand ? 1u : 0u;
+                        if (__reduce_add_sync(kFull, cnt) >= r.k_eff) tt = cand;
+                    }
+                    if (lane == 0) c.bc_u32[0] = tt;
+                }
+                cbar();
+                mkth = max(mkth, c.bc_u32[0]);
+            }
             if (a.mode == kModeShardTopK) rflags &= ~kFInf;
             uint32_t rkeep = 0;
             if (!(rflags & (kFTimeout | kFInf | kFOverflow))) {
                 uint32_t th = mkth;
                 if (r.minp) th = max(th, minp_key(mtop, r));
-                // every entry (flattened over the segments, a handful per
-                // thread, all loads in flight at once) at or above th
-                constexpr int kPer = kBuf / kCons;
-                uint64_t e[kPer];
+                // Entries at or above th.  The lists are sorted: a segment whose
+                // second entry is below th contributes at most its first (both
+                // are in registers); the rest of the others' lists are read in
+                // one flattened pass (a handful per thread, all in flight).
+                bool over = false;
+                over |= warp_push(tid < S && my_len > 0 && my_top >= th, top64, cand, kBuf, &c.n_cand);
+                over |= warp_push(tid < S && my_len > 1 && my_2nd >= th, snd64, cand, kBuf, &c.n_cand);
+                const uint32_t rem = (tid < S && my_len > 2 && my_2nd >= th) ? my_len - 2 : 0u;
+                uint32_t n_rem;
+                const uint32_t rem_off = cscan_excl(rem, &n_rem, c);
+                if (n_rem) {
+                    if (tid < S) c.hist[tid] = rem_off;
+                    cbar();
+                    constexpr int kPer = kBuf / kCons;
+                    uint64_t e[kPer];
 #pragma unroll
-                for (int j = 0; j < kPer; ++j) {
-                    const uint32_t idx = tid + j * kCons;
-                    e[j] = 0ull;
-                    if (idx < rtotal && idx < kBuf) {
-                        uint32_t lo = 0, hi = S - 1;  // last segment starting at or before idx
-                        while (lo < hi) {
-                            const uint32_t mid = (lo + hi + 1) / 2;
-                            if (c.hist[mid] <= idx) lo = mid;
-                            else hi = mid - 1;
+                    for (int j = 0; j < kPer; ++j) {
+                        const uint32_t idx = tid + j * kCons;
+                        e[j] = 0ull;
+                        if (idx < n_rem && idx < kBuf) {
+                            uint32_t lo = 0, hi = S - 1;  // last segment starting at or before idx
+                            while (lo < hi) {
+                                const uint32_t mid = (lo + hi + 1) / 2;
+                                if (c.hist[mid] <= idx) lo = mid;
+                                else hi = mid - 1;
+                            }
+                            e[j] = __ldcg(reinterpret_cast<const unsigned long long*>(
+                                a.seg_keys + static_cast<size_t>(v * S + lo) * kSegCap + 2 +
+                                (idx - c.hist[lo])));
                         }
-                        e[j] = __ldcg(reinterpret_cast<const unsigned long long*>(
-                            a.seg_keys + static_cast<size_t>(v * S + lo) * kSegCap + (idx - c.hist[lo])));
+                    }
+                    over |= n_rem > kBuf;
+#pragma unroll
+                    for (int j = 0; j < kPer; ++j) {
+                        const uint32_t idx = tid + j * kCons;
+                        const bool keep = idx < n_rem && idx < kBuf &&
+                                          static_cast<uint32_t>(e[j] >> 32) >= th;
+                        over |= warp_push(keep, e[j], cand, kBuf, &c.n_cand);
                     }
                 }
-                bool over = rtotal > kBuf;
-#pragma unroll
-                for (int j = 0; j < kPer; ++j) {
-                    const uint32_t idx = tid + j * kCons;
-                    const bool keep = idx < rtotal && idx < kBuf && static_cast<uint32_t>(e[j] >> 32) >= th;
-                    over |= warp_push(keep, e[j], cand, kBuf, &c.n_cand);
-                }
                 over = cbar_or(over);
+                Q38S_TT(u, 6);
                 const uint32_t nm = min(c.n_cand, kBuf);
                 if (over) rflags |= kFOverflow;  // more than the buffer holds
                 if (!(rflags & kFOverflow)) {
                     rkeep = finish_buffer(cand, nm, r, sorted, c, true);
                     if (rkeep == 0xffffffffu) rflags |= kFOverflow;
                 }
+                Q38S_TT(u, 10);
+                Q38S_TR(u, 14, nm);
             }
             if (tid == 0) a.row_ticket[v] = 0;  // every segment has arrived: reset for the next call
             Q38S_TR(u, 8, 4 + ((rflags & kFOverflow) ? 1 : 0));
