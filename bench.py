@@ -354,7 +354,8 @@ def batch1_latency(dev, stream):
                      "p50_us": float(rank(50)), "p99_us": float(rank(99)),
                      "mean_us": float(lat.mean()), "device_us": dev_ms * 1e3,
                      "call": "q38s_sampler_prepare_device (host wall time per call, incl. "
-                             "launch, 24-byte decision read-back and stream sync)",
+                             "launch and the wait for the 24-byte decision, which the kernel "
+                             "writes into mapped host memory)",
                      "target_us": 20.0}
     return out
 

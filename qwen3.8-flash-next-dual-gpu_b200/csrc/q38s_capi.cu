@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <chrono>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -526,8 +527,8 @@ struct q38s_sampler {
     int32_t* d_tokens = nullptr;       // commit / extra token staging
     uint32_t token_cap = 0;
     uint32_t* d_offsets = nullptr;     // {0, n}
-    q38s_decision_v1* d_decision = nullptr;
-    q38s_decision_v1* h_decision = nullptr;  // pinned
+    q38s_decision_v1* d_decision = nullptr;  // device view of h_decision
+    q38s_decision_v1* h_decision = nullptr;  // pinned, mapped: the kernel writes it directly
     int32_t* h_tokens = nullptr;             // pinned
     uint32_t* h_offsets = nullptr;           // pinned
 };
@@ -542,7 +543,6 @@ void free_sampler(q38s_sampler* s) {
         cudaFree(s->d_logits);
         cudaFree(s->d_tokens);
         cudaFree(s->d_offsets);
-        cudaFree(s->d_decision);
         cudaFreeHost(s->h_decision);
         cudaFreeHost(s->h_tokens);
         cudaFreeHost(s->h_offsets);
@@ -590,8 +590,11 @@ int sampler_create(int device, uint32_t vocabulary, const q38s_sampling_config_v
     cudaError_t e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&s->d_logits, sizeof(uint16_t) * static_cast<size_t>(vocabulary));
     if (e == cudaSuccess) e = cudaMalloc(&s->d_offsets, sizeof(uint32_t) * 2);
-    if (e == cudaSuccess) e = cudaMalloc(&s->d_decision, sizeof(q38s_decision_v1));
-    if (e == cudaSuccess) e = cudaMallocHost(&s->h_decision, sizeof(q38s_decision_v1));
+    if (e == cudaSuccess)
+        e = cudaHostAlloc(reinterpret_cast<void**>(&s->h_decision), sizeof(q38s_decision_v1),
+                          cudaHostAllocMapped);
+    if (e == cudaSuccess)
+        e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&s->d_decision), s->h_decision, 0);
     if (e == cudaSuccess) e = cudaMallocHost(&s->h_offsets, sizeof(uint32_t) * 2);
     if (e != cudaSuccess) {
         free_sampler(s);
@@ -623,6 +626,9 @@ int stage_tokens(q38s_sampler* s, const int32_t* tokens, size_t n) {
     return Q38S_OK;
 }
 
+// Status of a decision the kernel has not written yet (no Q38S_ROW_* value).
+constexpr int32_t kStatusPending = INT32_MIN;
+
 int prepare_common(const q38s_sampler* cs, const void* d_logits, uint16_t dtype, size_t count,
                    const int32_t* extra, size_t n_extra, q38s_decision_v1* out,
                    cudaStream_t stream, bool host_logits, const void* h_logits) {
@@ -647,22 +653,35 @@ int prepare_common(const q38s_sampler* cs, const void* d_logits, uint16_t dtype,
         Q38S_CUDA(cudaMemcpyAsync(s->d_logits, h_logits, sizeof(uint16_t) * count,
                                   cudaMemcpyHostToDevice, s->stream),
                   "logits upload");
-    int rc = stage_tokens(s, extra, n_extra);
+    int rc = n_extra ? stage_tokens(s, extra, n_extra) : Q38S_OK;  // nothing to upload without
     if (rc) return rc;
     SampleArgs a = base_args(s->batch, host_logits ? s->d_logits : d_logits, dtype, count);
+    // The kernel writes the decision into mapped host memory, status last;
+    // the host waits for the status to change (bounded), so a call costs no
+    // read-back copy and no stream synchronisation on the common path.
     a.decisions = s->d_decision;
+    a.decisions_host = 1;
     if (n_extra) {
         a.extra_mode = 1;
         a.extra_tokens = s->d_tokens;
         a.extra_offsets = s->d_offsets;
     }
+    volatile q38s_decision_v1* hd = s->h_decision;
+    hd->status = kStatusPending;
     rc = launch_checked(a, s->stream, "prepare", s->batch->device);
     if (rc) return rc;
-    Q38S_CUDA(cudaMemcpyAsync(s->h_decision, s->d_decision, sizeof(q38s_decision_v1),
-                              cudaMemcpyDeviceToHost, s->stream),
-              "decision readback");
-    Q38S_CUDA(cudaStreamSynchronize(s->stream), "prepare");
-    const q38s_decision_v1 d = *s->h_decision;
+    const auto t_start = std::chrono::steady_clock::now();
+    for (uint32_t spin = 1; hd->status == kStatusPending; ++spin) {
+        if ((spin & 1023u) == 0 &&
+            std::chrono::steady_clock::now() - t_start > std::chrono::milliseconds(200))
+            break;  // long or failed: the stream reports it
+    }
+    if (hd->status == kStatusPending) Q38S_CUDA(cudaStreamSynchronize(s->stream), "prepare");
+    q38s_decision_v1 d;
+    d.token = hd->token;
+    d.status = hd->status;
+    d.rng_before = hd->rng_before;
+    d.rng_after = hd->rng_after;
     switch (d.status) {
         case Q38S_ROW_OK: break;
         case Q38S_ROW_NO_FINITE: return fail(Q38S_RUNTIME_ERROR, kMsgNoFinite);

@@ -69,6 +69,7 @@ struct SampleArgs {
     const uint32_t* extra_offsets;
     // outputs
     q38s_decision_v1* decisions;
+    int decisions_host;   // decisions is mapped host memory: status is written last
     q38s_distribution dist;
     q38s_candidate* topk_out;  // kModeShardTopK: vrows * k_out entries
     uint32_t k_out;

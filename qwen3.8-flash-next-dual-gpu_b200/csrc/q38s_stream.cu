@@ -711,7 +711,17 @@ __device__ void write_decision(const SampleArgs& a, const Row& r, int32_t token,
     d.status = status;
     d.rng_before = r.rng_before;
     d.rng_after = r.rng_before + kGamma;
-    if (a.decisions) a.decisions[r.v] = d;
+    if (a.decisions && a.decisions_host) {
+        // a host that polls the status sees the other fields first
+        volatile q38s_decision_v1* p = a.decisions + r.v;
+        p->token = d.token;
+        p->rng_before = d.rng_before;
+        p->rng_after = d.rng_after;
+        __threadfence_system();
+        p->status = d.status;
+    } else if (a.decisions) {
+        a.decisions[r.v] = d;
+    }
     if (a.mode == kModeSampleCommit && status == Q38S_ROW_OK) {
         // commit (sampling.cc:148-156) then commit_token (sampling.cc:163-172)
         // (the state was read at the start of the row; only this row's
