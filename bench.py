@@ -277,8 +277,8 @@ def run_ours(args, rank, world, dist):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "frac_of_8tbs_nominal": achieved / 8000.0,
-                     "traffic": load_traffic("cfg4_sample_rows_bf16"),
-                     "kernel": "sample_rows_kernel<bf16> (one launch per step)",
+                     "traffic": load_traffic("cfg4_stream_kernel_bf16"),
+                     "kernel": "stream_kernel<bf16> (one launch per step)",
                      "algorithmic_bytes_per_launch": algo_bytes},
         "clocks": clk,
     }
