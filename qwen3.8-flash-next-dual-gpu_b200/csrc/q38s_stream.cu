@@ -50,7 +50,8 @@ namespace q38s {
 namespace {
 
 constexpr uint32_t kTileBytes = 16384;           // logits per ring slot
-constexpr uint32_t kSlot = kTileBytes;
+constexpr uint32_t kTileBm = 1024;               // bitmap bytes per slot (8,192 columns)
+constexpr uint32_t kSlot = kTileBytes + kTileBm;
 constexpr uint32_t kRing = 4;                    // ring slots per CTA
 constexpr int kCons = 256;                       // consumer threads (warps 0-7)
 constexpr int kBlock = kCons + 32;               // + the producer warp
@@ -796,7 +797,9 @@ __device__ void row_output(const SampleArgs& a, const Row& r, const uint64_t* so
         return;
     }
     epilogue(sorted, keep, r.p, r.minp, r.rng_before, w, S, q, c);
+    Q38S_TT(r.v, 11);
     write_decision(a, r, c.e_token, c.e_status);
+    Q38S_TT(r.v, 12);
     write_distribution(a, r, sorted, w, c);
 }
 
@@ -1286,7 +1289,10 @@ __device__ void produce(const SampleArgs& a, unsigned char* ring, Ctl& c) {
         uint32_t c0, c1;
         chunk_range(a.vocab, S, u % S, c0, c1);
         if (!unit_streams(a, v, c1 - c0, TC)) continue;
+        const uint32_t srow = state_row(a, v);
+        const bool pen = (a.params[srow].flags & kFlagPenalties) != 0;
         const unsigned char* row = row_ptr<DT>(a, v);
+        const uint32_t* bmrow = a.bitmap + static_cast<size_t>(srow) * a.bitmap_words;
         for (uint32_t t0 = c0; t0 < c1; t0 += TC, ++g) {
             const uint32_t slot = g % kRing;
             if (g >= kRing) {
@@ -1307,9 +1313,13 @@ __device__ void produce(const SampleArgs& a, unsigned char* ring, Ctl& c) {
             const uint32_t n = min(c1 - t0, TC);
             const uint32_t bytes = n * es;
             const uint32_t bulk = a.use_tma ? (bytes & ~15u) : 0u;
+            // the tile's slice of the penalty bitmap rides along (the stream
+            // reads the penalty bit of each thread's largest element)
+            const uint32_t bmb = pen ? ((n + 127) / 128) * 16 : 0u;
             unsigned char* sl = ring + slot * kSlot;
-            mbar_arrive_expect_tx(&c.full[slot], bulk);
+            mbar_arrive_expect_tx(&c.full[slot], bulk + bmb);
             if (bulk) tma_load_1d(sl, row + static_cast<size_t>(t0) * es, bulk, &c.full[slot]);
+            if (bmb) tma_load_1d(sl + kTileBytes, bmrow + t0 / 32, bmb, &c.full[slot]);
             atomicExch(&c.issued, g + 1);
         }
     }
@@ -1389,7 +1399,9 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
 #endif
         }
         float tmax = -INFINITY;  // the thread's largest raw value ...
-        uint32_t tmax_t = 0;     // ... and its tile
+        uint32_t tcol = 0;       // ... the first column holding it
+        uint32_t tpen = 0;       // ... and that column's bit of the state row's bitmap
+        bool tnan = false;       // some block of the thread has only NaN maxima
         for (uint32_t t = 0; streams && t < ntiles; ++t, ++g) {
             const uint32_t slot = g % kRing;
             unsigned char* sl = ring + slot * kSlot;
@@ -1459,9 +1471,28 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             // bf16 rounded up: an upper bound of every element of the block
             bkey[t * kCons + tid] = __bfloat16_as_ushort(__float2bfloat16_ru(bm));
             if (bm > tmax) {
+                // a new largest value: its first element (vector, then lane
+                // of the vector) and penalty bit, from the slot
                 tmax = bm;
-                tmax_t = t;
+                const uint32_t* sbm = reinterpret_cast<const uint32_t*>(sl + kTileBytes);
+                uint32_t jm = 0xffffffffu;
+#pragma unroll
+                for (int q = kU - 1; q >= 0; --q) {
+                    const uint32_t j = tid + q * kCons;
+                    if (j < nvec && vec_max<DT>(vec[j]) == bm) jm = j;
+                }
+                if (jm != 0xffffffffu) {
+                    const uint4 w = vec[jm];
+                    uint32_t e = 0;
+#pragma unroll
+                    for (int i = static_cast<int>(pv) - 1; i >= 0; --i)
+                        if (vec_elem<DT>(w, i) == bm) e = static_cast<uint32_t>(i);
+                    const uint32_t idx = jm * pv + e;
+                    tcol = t0 + idx;
+                    tpen = r.pen ? (sbm[idx >> 5] >> (idx & 31)) & 1u : 0u;
+                }
             }
+            tnan |= bm != bm;
 #ifdef Q38S_TRACE
             if (g_trace && u < 256 && t < 20 && lane == 0 && warp == 0)
                 g_trace[119808 + static_cast<size_t>(u) * 20 + t] =
@@ -1473,46 +1504,16 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(&c.empty[slot]);
         }
-        // ---- the exact value of the thread's largest element (found again
-        // among its vectors of tile tmax_t; one element per thread keeps the
-        // k-th largest key a lower bound of the row's), before the barrier
-        // so that its loads overlap the other warps' last tiles
+        // ---- the exact value of the thread's largest element (one element
+        // per thread keeps the k-th largest key a lower bound of the row's)
         uint32_t tk = 0;
         if (streams && !stop && tmax > -INFINITY) {
-            const uint32_t t0 = c0 + tmax_t * TC;
-            const uint32_t n = min(c1 - t0, TC);
-            uint32_t col = 0xffffffffu, pwc = 0;
-            float x = 0.0f;
-            uint4 w[kU];
-            uint32_t pw[kU];
-#pragma unroll
-            for (int q = 0; q < kU; ++q) {  // every load in flight at once
-                const uint32_t e0 = (tid + q * kCons) * pv;
-                const uint32_t nv = e0 < n ? min(pv, n - e0) : 0u;
-                w[q] = nv ? load_vec<DT>(a, src_row, t0 + e0, nv)
-                          : make_uint4(0u, 0u, 0u, 0u);
-                pw[q] = (nv && r.pen) ? __ldg(&r.gbm[(t0 + e0) >> 5]) : 0u;
-            }
-#pragma unroll
-            for (int q = 0; q < kU; ++q) {
-                const uint32_t e0 = (tid + q * kCons) * pv;
-#pragma unroll
-                for (uint32_t e = 0; e < pv; ++e) {
-                    const float xe = vec_elem<DT>(w[q], static_cast<int>(e));
-                    if (col == 0xffffffffu && e0 + e < n && xe == tmax) {
-                        col = t0 + e0 + e;
-                        x = xe;
-                        pwc = pw[q];
-                    }
-                }
-            }
-            if (col != 0xffffffffu) {
-                const float vx = exact_pw(a, r, x, col, pwc);
-                if (vx == INFINITY) atomicOr(&c.flags, kFInf);
-                tk = float_key(vx);
-            }
+            const float vx = exact_pw(a, r, tmax, tcol, tpen << (tcol & 31));
+            if (vx == INFINITY) atomicOr(&c.flags, kFInf);
+            tk = float_key(vx);
         }
         c.tkey[tid] = tk;
+        Q38S_TT(u, 15);
         const bool any_stop = cbar_or(stop);  // also publishes the keys
         Q38S_TT(u, 2);
         uint32_t theta = 0;
@@ -1577,11 +1578,14 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                 }
             };
             // the thread's tiles whose bound reaches rho (a NaN bound counts)
+            // (no bound of a thread exceeds its largest value rounded up)
             uint64_t hm = 0;
+            if (tnan || !(__bfloat162float(__float2bfloat16_ru(tmax)) < rho)) {
 #pragma unroll 4
-            for (uint32_t t = 0; t < ntiles; ++t) {
-                const float bound = __bfloat162float(__ushort_as_bfloat16(bkey[t * kCons + tid]));
-                if (!(bound < rho)) hm |= 1ull << t;
+                for (uint32_t t = 0; t < ntiles; ++t) {
+                    const float bound = __bfloat162float(__ushort_as_bfloat16(bkey[t * kCons + tid]));
+                    if (!(bound < rho)) hm |= 1ull << t;
+                }
             }
 #ifdef Q38S_TRACE
             atomicAdd(&c.bc_u32[3], __popcll(hm));
