@@ -186,6 +186,10 @@ int create_batch(int device, uint32_t full_vocab, uint32_t col_begin, uint32_t c
     if (rows == 0 || !configs) return fail(Q38S_INVALID_ARGUMENT, kMsgDims);
     if (columns == 0 || static_cast<uint64_t>(col_begin) + columns > full_vocab)
         return fail(Q38S_INVALID_ARGUMENT, kMsgDims);
+    // the general path's fixed-point masses (2^43 per token) sum without
+    // overflow up to 2^20 columns
+    if (columns > kMaxGeneralVocab)
+        return fail(Q38S_INVALID_ARGUMENT, "more than 1,048,576 columns per batch");
     for (uint32_t r = 0; r < rows; ++r) {
         const int rc = validate_config(full_vocab, version, configs[r]);
         if (rc) return rc;

@@ -1,4 +1,4 @@
-// Kernel-side data structures shared by q38s_sample.cu and the host ABI.
+// Kernel-side data structures shared by the kernels and the host ABI.
 #pragma once
 
 #include <stddef.h>
@@ -9,13 +9,8 @@
 
 namespace q38s {
 
-constexpr int kThreads = 256;        // threads per CTA
-constexpr int kMaxCluster = 8;       // CTAs per row (portable cluster size)
-constexpr int kCap = 1024;           // per-CTA candidate buffer (rank keys)
-constexpr int kLeaderCap = 1024;     // merged candidates held by the leader
-constexpr int kFastTopK = 128;       // largest top_k served by the fast path
-constexpr int kPieces = 4;           // TMA pieces per chunk
-constexpr int kHistBins = 256;       // radix digit histogram (general path)
+constexpr int kThreads = 256;        // threads per CTA of the small kernels
+constexpr int kLeaderCap = 1024;     // candidates of a distribution / shard list
 constexpr uint32_t kMaxGeneralVocab = 1u << 20;  // fixed-point mass headroom
 
 // Per-row mutable sampler state: SamplerStateV1 (sampling.h:31-39) minus
@@ -97,10 +92,9 @@ struct SampleArgs {
 constexpr uint32_t kSegCap = 512;       // candidates a segment hands to the merge
 constexpr uint32_t kMaxSegUnits = 512;  // vrows * segs when segs > 1
 
-// Launchers (q38s_sample.cu).  All return a cudaError_t as int.
+// Launchers (q38s_stream.cu, q38s_sample.cu).  All return a cudaError_t as int.
 int launch_stream(const SampleArgs& a, void* stream);   // streaming sampler
 uint32_t stream_segments(uint32_t vrows, uint32_t vocab, int device);
-int launch_sample(const SampleArgs& a, void* stream);
 int launch_commit_tokens(RowState* state, uint32_t* bitmap, uint32_t bitmap_words,
                          uint32_t* counts, uint32_t vocab, uint32_t col_begin,
                          uint32_t rows, const int32_t* tokens, const uint32_t* offsets,
@@ -114,7 +108,5 @@ int launch_shard_merge(const RowParams* params, const RowState* state, uint32_t 
                        uint32_t k_local, q38s_decision_v1* decisions, void* stream);
 int launch_argmax_bf16(const uint16_t* logits, uint32_t count, int32_t* out,
                        void* stream);
-size_t sample_smem_bytes(uint32_t vocab, int dtype, int cluster);
-int sample_cluster_size(uint32_t vocab);
 
 }  // namespace q38s
