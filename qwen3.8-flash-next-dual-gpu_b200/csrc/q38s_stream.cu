@@ -804,102 +804,182 @@ __device__ void row_output(const SampleArgs& a, const Row& r, const uint64_t* so
 }
 
 // Speculative verification over all virtual rows' distributions (target
-// rows 0..n, draft rows n+1..2n); one thread of the CTA that finished the
-// last row.  Leviathan et al. 2023 / Chen et al. 2023 rejection sampling:
-// draft i is accepted iff u_i * q_i(d_i) < p_i(d_i) with u_i =
-// uniform01(s_i ^ kAcceptDomain), s_i = rng_state + (i + 1) * gamma; the
-// first rejection draws from max(0, p_i - q_i) over p_i's sorted support
-// with uniform01(s_i); if every draft is accepted the bonus token is the
-// reference draw from p_n.  Other CTAs wrote these arrays: L2 loads.
-__device__ void mtp_finish(const SampleArgs& a) {
-    q38s_mtp_result res;
+// rows 0..n, draft rows n+1..2n), by the whole CTA that finished the last
+// row.  Leviathan et al. 2023 / Chen et al. 2023 rejection sampling: draft
+// i is accepted iff u_i * q_i(d_i) < p_i(d_i) with u_i = uniform01(s_i ^
+// kAcceptDomain), s_i = rng_state + (i + 1) * gamma; the first rejection
+// draws from max(0, p_i - q_i) over p_i's sorted support with
+// uniform01(s_i); if every draft is accepted the bonus token is the
+// reference draw from p_n.  The probability lookups run in parallel (four
+// threads per draft, then one thread per support entry); the ordered walk
+// over the drafts and the sequential sums of the residual draw run in one
+// thread, in the order written here.  Other CTAs wrote the arrays read
+// here: L2 loads.
+__device__ void mtp_finish(const SampleArgs& a, unsigned char* area, Ctl& c) {
     const uint32_t n = a.n_draft;
     const uint32_t cap = a.dist.capacity;
+    const uint32_t tid = threadIdx.x;
     const uint64_t rng0 = __ldcg(reinterpret_cast<const unsigned long long*>(
         &a.state[a.vrow_state_const].rng_state));
-    res.rng_before = rng0;
-    res.status = Q38S_ROW_OK;
-    res.n_tokens = 0;
-    res.n_accepted = 0;
-    for (uint32_t i = 0; i <= n; ++i) {
-        const int32_t t_status = __ldcg(&a.decisions[i].status);
-        const int32_t t_token = __ldcg(&a.decisions[i].token);
-        const uint64_t s_i = rng0 + (static_cast<uint64_t>(i) + 1) * kGamma;
-        if (t_status != Q38S_ROW_OK) {
-            res.status = t_status;
-            break;
+    // phase-one layout of the area: result, per-draft p(d), q(d), flags, row headers
+    q38s_mtp_result* rs = reinterpret_cast<q38s_mtp_result*>(area);
+    double* pd = reinterpret_cast<double*>(area + 512);
+    double* qd = pd + 64;
+    uint32_t* acc = reinterpret_cast<uint32_t*>(qd + 64);
+    int32_t* hs = reinterpret_cast<int32_t*>(acc + 64);  // row i: t_status, t_token, d_status, np, nq, d
+    if (tid <= n) {
+        int32_t* h = hs + tid * 6;
+        h[0] = __ldcg(&a.decisions[tid].status);
+        h[1] = __ldcg(&a.decisions[tid].token);
+        if (tid < n) {
+            h[2] = __ldcg(&a.decisions[n + 1 + tid].status);
+            h[3] = static_cast<int32_t>(__ldcg(&a.dist.n_retained[tid]));
+            h[4] = static_cast<int32_t>(__ldcg(&a.dist.n_retained[n + 1 + tid]));
+            h[5] = a.draft_tokens[tid];
         }
-        if (i == n) {  // bonus row: the reference draw from p_n
-            res.tokens[res.n_tokens++] = t_token;
-            break;
-        }
-        const int32_t d_status = __ldcg(&a.decisions[n + 1 + i].status);
-        if (d_status != Q38S_ROW_OK) {
-            res.status = d_status;
-            break;
-        }
-        const uint32_t np = __ldcg(&a.dist.n_retained[i]);
-        const uint32_t nq = __ldcg(&a.dist.n_retained[n + 1 + i]);
-        if (np > cap || nq > cap || np == 0) {
-            res.status = Q38S_ROW_NORMALIZATION;
-            break;
-        }
-        const int32_t* pt = a.dist.tokens + static_cast<size_t>(i) * cap;
-        const double* pp = a.dist.probs + static_cast<size_t>(i) * cap;
-        const int32_t* qt = a.dist.tokens + static_cast<size_t>(n + 1 + i) * cap;
-        const double* qp = a.dist.probs + static_cast<size_t>(n + 1 + i) * cap;
-        const int32_t d = a.draft_tokens[i];
-        double pd = 0.0, qd = 0.0;
-        for (uint32_t j = 0; j < np; ++j)
-            if (__ldcg(&pt[j]) == d) pd = __ldcg(&pp[j]);
-        for (uint32_t j = 0; j < nq; ++j)
-            if (__ldcg(&qt[j]) == d) qd = __ldcg(&qp[j]);
-        const double ua = uniform01(s_i ^ kAcceptDomain);
-        if (ua * qd < pd) {
-            res.tokens[res.n_tokens++] = d;
-            ++res.n_accepted;
-            continue;
-        }
-        auto q_of = [&](int32_t tok) {
-            double qj = 0.0;
-            for (uint32_t m = 0; m < nq; ++m)
-                if (__ldcg(&qt[m]) == tok) qj = __ldcg(&qp[m]);
-            return qj;
-        };
-        double rtotal = 0.0;
-        for (uint32_t j = 0; j < np; ++j) rtotal += fmax(0.0, __ldcg(&pp[j]) - q_of(__ldcg(&pt[j])));
-        int32_t tok = t_token;  // empty residual: the reference draw from p_i
-        if (rtotal > 0.0) {
-            const double draw = uniform01(s_i) * rtotal;
-            double cum = 0.0;
-            uint32_t sel = np - 1;
-            for (uint32_t j = 0; j < np; ++j) {
-                cum += fmax(0.0, __ldcg(&pp[j]) - q_of(__ldcg(&pt[j])));
-                if (draw < cum) {
-                    sel = j;
-                    break;
-                }
-            }
-            tok = __ldcg(&pt[sel]);
-        }
-        res.tokens[res.n_tokens++] = tok;
-        break;
     }
-    res.rng_after = res.rng_before + static_cast<uint64_t>(res.n_tokens) * kGamma;
-    *a.mtp = res;
+    if (tid < 64) {
+        pd[tid] = 0.0;
+        qd[tid] = 0.0;
+    }
+    cbar();
+    // p_i(d_i) and q_i(d_i): draft i = tid % 64, list entries sub, sub + 4, ...
+    {
+        const uint32_t i = tid & 63u, sub = tid >> 6;
+        if (i < n) {
+            const int32_t* h = hs + i * 6;
+            const uint32_t np = static_cast<uint32_t>(h[3]), nq = static_cast<uint32_t>(h[4]);
+            if (h[0] == Q38S_ROW_OK && h[2] == Q38S_ROW_OK && np <= cap && nq <= cap) {
+                const int32_t d = h[5];
+                const int32_t* pt = a.dist.tokens + static_cast<size_t>(i) * cap;
+                const double* pp = a.dist.probs + static_cast<size_t>(i) * cap;
+                const int32_t* qt = a.dist.tokens + static_cast<size_t>(n + 1 + i) * cap;
+                const double* qp = a.dist.probs + static_cast<size_t>(n + 1 + i) * cap;
+#pragma unroll 4
+                for (uint32_t j = sub; j < np; j += 4)
+                    if (__ldcg(&pt[j]) == d) pd[i] = __ldcg(&pp[j]);
+#pragma unroll 4
+                for (uint32_t j = sub; j < nq; j += 4)
+                    if (__ldcg(&qt[j]) == d) qd[i] = __ldcg(&qp[j]);
+            }
+        }
+    }
+    cbar();
+    if (tid < n) {
+        const uint64_t s_i = rng0 + (static_cast<uint64_t>(tid) + 1) * kGamma;
+        acc[tid] = uniform01(s_i ^ kAcceptDomain) * qd[tid] < pd[tid] ? 1u : 0u;
+    }
+    cbar();
+    // the drafts in order (one thread, shared memory only)
+    if (tid == 0) {
+        rs->rng_before = rng0;
+        rs->status = Q38S_ROW_OK;
+        rs->n_tokens = 0;
+        rs->n_accepted = 0;
+        uint32_t rej = 0xffffffffu;
+        for (uint32_t i = 0; i <= n; ++i) {
+            const int32_t* h = hs + i * 6;
+            if (h[0] != Q38S_ROW_OK) {
+                rs->status = h[0];
+                break;
+            }
+            if (i == n) {  // bonus row: the reference draw from p_n
+                rs->tokens[rs->n_tokens++] = h[1];
+                break;
+            }
+            if (h[2] != Q38S_ROW_OK) {
+                rs->status = h[2];
+                break;
+            }
+            const uint32_t np = static_cast<uint32_t>(h[3]), nq = static_cast<uint32_t>(h[4]);
+            if (np > cap || nq > cap || np == 0) {
+                rs->status = Q38S_ROW_NORMALIZATION;
+                break;
+            }
+            if (acc[i]) {
+                rs->tokens[rs->n_tokens++] = h[5];
+                ++rs->n_accepted;
+                continue;
+            }
+            rej = i;
+            break;
+        }
+        c.bc_u32[0] = rej;
+        if (rej != 0xffffffffu) {
+            c.bc_u32[1] = static_cast<uint32_t>(hs[rej * 6 + 3]);
+            c.bc_u32[2] = static_cast<uint32_t>(hs[rej * 6 + 4]);
+            c.bc_u32[3] = static_cast<uint32_t>(hs[rej * 6 + 1]);
+        }
+    }
+    cbar();
+    const uint32_t rej = c.bc_u32[0];
+    if (rej != 0xffffffffu) {
+        // residual max(0, p_i - q_i) over p_i's support: the lists in shared
+        // memory (the phase-one arrays are dead now), one thread per entry
+        const uint32_t np = c.bc_u32[1], nq = c.bc_u32[2];
+        const int32_t t_token = static_cast<int32_t>(c.bc_u32[3]);
+        int32_t* ptl = reinterpret_cast<int32_t*>(area + 512);
+        int32_t* qtl = ptl + kLeaderCap;
+        double* ppl = reinterpret_cast<double*>(qtl + kLeaderCap);
+        double* qpl = ppl + kLeaderCap;
+        const size_t prow = static_cast<size_t>(rej) * cap;
+        const size_t qrow = static_cast<size_t>(n + 1 + rej) * cap;
+        for (uint32_t j = tid; j < np; j += kCons) {
+            ptl[j] = __ldcg(&a.dist.tokens[prow + j]);
+            ppl[j] = __ldcg(&a.dist.probs[prow + j]);
+        }
+        for (uint32_t j = tid; j < nq; j += kCons) {
+            qtl[j] = __ldcg(&a.dist.tokens[qrow + j]);
+            qpl[j] = __ldcg(&a.dist.probs[qrow + j]);
+        }
+        cbar();
+        for (uint32_t j = tid; j < np; j += kCons) {
+            double qj = 0.0;
+            const int32_t tok = ptl[j];
+            for (uint32_t m = 0; m < nq; ++m)
+                if (qtl[m] == tok) qj = qpl[m];
+            ppl[j] = fmax(0.0, ppl[j] - qj);  // in place: entry j is this thread's
+        }
+        cbar();
+        if (tid == 0) {
+            const uint64_t s_i = rng0 + (static_cast<uint64_t>(rej) + 1) * kGamma;
+            double rtotal = 0.0;
+            for (uint32_t j = 0; j < np; ++j) rtotal += ppl[j];
+            int32_t tok = t_token;  // empty residual: the reference draw from p_i
+            if (rtotal > 0.0) {
+                const double draw = uniform01(s_i) * rtotal;
+                double cum = 0.0;
+                uint32_t sel = np - 1;
+                for (uint32_t j = 0; j < np; ++j) {
+                    cum += ppl[j];
+                    if (draw < cum) {
+                        sel = j;
+                        break;
+                    }
+                }
+                tok = ptl[sel];
+            }
+            rs->tokens[rs->n_tokens++] = tok;
+        }
+    }
+    if (tid == 0) {
+        rs->rng_after = rs->rng_before + static_cast<uint64_t>(rs->n_tokens) * kGamma;
+        *a.mtp = *rs;
+    }
+    cbar();
 }
 
 // A virtual row is complete: the last one runs the speculative verification.
-__device__ void row_done(const SampleArgs& a, Ctl& c) {
+__device__ void row_done(const SampleArgs& a, unsigned char* area, Ctl& c) {
     if (!a.mtp) return;
-    __threadfence();
     cbar();
-    if (threadIdx.x == 0) c.bc_u32[2] = atomicAdd(a.ticket, 1u) == a.vrows - 1;
+    // one GPU-scope acquire-release ticket (see the segment merge)
+    if (threadIdx.x == 0)
+        c.bc_u32[2] = atom_add_acq_rel_gpu(a.ticket, 1u) == a.vrows - 1;
     cbar();
-    if (c.bc_u32[2] && threadIdx.x == 0) {
-        __threadfence();
-        *a.ticket = 0;
-        mtp_finish(a);
+    if (c.bc_u32[2]) {
+        if (threadIdx.x == 0) *a.ticket = 0;
+        mtp_finish(a, area, c);
     }
 }
 
@@ -1252,7 +1332,7 @@ __device__ void finish_row(const SampleArgs& a, const Row& r, uint32_t flags,
         double* w = reinterpret_cast<double*>(area + (kBuf + kFinal) * 8);
         row_output(a, r, sorted, keep, w, w + kFinal, w + 2 * kFinal, c);
     }
-    row_done(a, c);
+    row_done(a, area, c);
 }
 
 // ------------------------------------------------------------ the kernel
