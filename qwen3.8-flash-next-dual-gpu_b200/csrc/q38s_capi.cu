@@ -146,10 +146,6 @@ struct q38s_batch {
     uint32_t* d_mtp_ncand = nullptr;
     q38s_decision_v1* d_mtp_dec = nullptr;
     uint32_t* d_ticket = nullptr;
-    // streaming sampler: per-unit segment lists and per-virtual-row tickets
-    uint64_t* d_seg_keys = nullptr;
-    uint32_t* d_seg_hdr = nullptr;
-    uint32_t* d_row_ticket = nullptr;
 };
 
 namespace {
@@ -172,9 +168,6 @@ void free_batch(q38s_batch* b) {
     cudaFree(b->d_mtp_ncand);
     cudaFree(b->d_mtp_dec);
     cudaFree(b->d_ticket);
-    cudaFree(b->d_seg_keys);
-    cudaFree(b->d_seg_hdr);
-    cudaFree(b->d_row_ticket);
     delete b;
 }
 
@@ -230,12 +223,6 @@ int create_batch(int device, uint32_t full_vocab, uint32_t col_begin, uint32_t c
     alloc(reinterpret_cast<void**>(&b->d_scratch),
           2 * sizeof(uint32_t) * static_cast<size_t>(columns) * rows);  // keys, weights
     b->scratch_rows = rows;
-    const size_t tickets = std::max<size_t>(rows, kMtpRows);
-    alloc(reinterpret_cast<void**>(&b->d_seg_keys),
-          sizeof(uint64_t) * static_cast<size_t>(kMaxSegUnits) * kSegCap);
-    alloc(reinterpret_cast<void**>(&b->d_seg_hdr), sizeof(uint32_t) * 4 * kMaxSegUnits);
-    alloc(reinterpret_cast<void**>(&b->d_row_ticket), sizeof(uint32_t) * tickets);
-    if (e == cudaSuccess) e = cudaMemset(b->d_row_ticket, 0, sizeof(uint32_t) * tickets);
     if (e == cudaSuccess)
         e = cudaMemcpy(b->d_params, params.data(), sizeof(RowParams) * rows,
                        cudaMemcpyHostToDevice);
@@ -291,9 +278,6 @@ SampleArgs base_args(const q38s_batch* b, const void* logits, uint16_t dtype,
     a.vrow_state_const = ~0u;
     a.scratch = b->d_scratch;
     a.scratch_w = reinterpret_cast<float*>(b->d_scratch + static_cast<size_t>(b->vocab) * b->rows);
-    a.seg_keys = b->d_seg_keys;
-    a.seg_hdr = b->d_seg_hdr;
-    a.row_ticket = b->d_row_ticket;
     return a;
 }
 
@@ -528,13 +512,19 @@ struct q38s_sampler {
     q38s_sampler_state_v1 state{};     // host mirror (authoritative)
     cudaStream_t stream = nullptr;
     void* d_logits = nullptr;          // staging for host logits (bf16)
-    int32_t* d_tokens = nullptr;       // commit / extra token staging
+    // token staging (commit_tokens, additional penalty tokens): {0, n}
+    // then the n tokens, uploaded with one copy from a pinned mirror
+    uint32_t* d_stage = nullptr;
+    uint32_t* h_stage = nullptr;             // pinned
     uint32_t token_cap = 0;
-    uint32_t* d_offsets = nullptr;     // {0, n}
+    uint32_t* d_offsets = nullptr;           // d_stage
+    int32_t* d_tokens = nullptr;             // d_stage + 2
+    uint32_t* h_offsets = nullptr;           // h_stage
+    int32_t* h_tokens = nullptr;             // h_stage + 2
+    cudaEvent_t staged = nullptr;            // the last upload out of h_stage
+    bool staged_pending = false;             // ... may not have run yet
     q38s_decision_v1* d_decision = nullptr;  // device view of h_decision
     q38s_decision_v1* h_decision = nullptr;  // pinned, mapped: the kernel writes it directly
-    int32_t* h_tokens = nullptr;             // pinned
-    uint32_t* h_offsets = nullptr;           // pinned
 };
 
 namespace {
@@ -545,11 +535,10 @@ void free_sampler(q38s_sampler* s) {
         DeviceGuard g(s->batch->device);
         if (s->stream) cudaStreamSynchronize(s->stream);
         cudaFree(s->d_logits);
-        cudaFree(s->d_tokens);
-        cudaFree(s->d_offsets);
+        cudaFree(s->d_stage);
         cudaFreeHost(s->h_decision);
-        cudaFreeHost(s->h_tokens);
-        cudaFreeHost(s->h_offsets);
+        cudaFreeHost(s->h_stage);
+        if (s->staged) cudaEventDestroy(s->staged);
         if (s->stream) cudaStreamDestroy(s->stream);
         free_batch(s->batch);
     }
@@ -560,13 +549,22 @@ int ensure_tokens(q38s_sampler* s, size_t n) {
     if (n <= s->token_cap) return Q38S_OK;
     uint32_t cap = std::max<uint32_t>(1024, s->token_cap);
     while (cap < n) cap *= 2;
-    cudaFree(s->d_tokens);
-    cudaFreeHost(s->h_tokens);
-    s->d_tokens = nullptr;
-    s->h_tokens = nullptr;
+    // queued work may still read the old buffers
+    if (s->stream) Q38S_CUDA(cudaStreamSynchronize(s->stream), "token staging");
+    s->staged_pending = false;
+    cudaFree(s->d_stage);
+    cudaFreeHost(s->h_stage);
+    s->d_stage = s->h_stage = s->d_offsets = s->h_offsets = nullptr;
+    s->d_tokens = s->h_tokens = nullptr;
     s->token_cap = 0;
-    Q38S_CUDA(cudaMalloc(&s->d_tokens, sizeof(int32_t) * cap), "token staging");
-    Q38S_CUDA(cudaMallocHost(&s->h_tokens, sizeof(int32_t) * cap), "token staging");
+    Q38S_CUDA(cudaMalloc(&s->d_stage, sizeof(uint32_t) * (2 + static_cast<size_t>(cap))),
+              "token staging");
+    Q38S_CUDA(cudaMallocHost(&s->h_stage, sizeof(uint32_t) * (2 + static_cast<size_t>(cap))),
+              "token staging");
+    s->d_offsets = s->d_stage;
+    s->h_offsets = s->h_stage;
+    s->d_tokens = reinterpret_cast<int32_t*>(s->d_stage + 2);
+    s->h_tokens = reinterpret_cast<int32_t*>(s->h_stage + 2);
     s->token_cap = cap;
     return Q38S_OK;
 }
@@ -593,13 +591,12 @@ int sampler_create(int device, uint32_t vocabulary, const q38s_sampling_config_v
     DeviceGuard g(device);
     cudaError_t e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&s->d_logits, sizeof(uint16_t) * static_cast<size_t>(vocabulary));
-    if (e == cudaSuccess) e = cudaMalloc(&s->d_offsets, sizeof(uint32_t) * 2);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->staged, cudaEventDisableTiming);
     if (e == cudaSuccess)
         e = cudaHostAlloc(reinterpret_cast<void**>(&s->h_decision), sizeof(q38s_decision_v1),
                           cudaHostAllocMapped);
     if (e == cudaSuccess)
         e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&s->d_decision), s->h_decision, 0);
-    if (e == cudaSuccess) e = cudaMallocHost(&s->h_offsets, sizeof(uint32_t) * 2);
     if (e != cudaSuccess) {
         free_sampler(s);
         return cuda_fail(e, "sampler allocation");
@@ -613,20 +610,23 @@ int sampler_create(int device, uint32_t vocabulary, const q38s_sampling_config_v
     return ok();
 }
 
-// Uploads n tokens into d_tokens and {0, n} into d_offsets on s->stream.
+// Uploads {0, n} and n tokens into d_stage on s->stream, one copy.  The
+// pinned mirror is rewritten only after the previous upload out of it ran.
 int stage_tokens(q38s_sampler* s, const int32_t* tokens, size_t n) {
     int rc = ensure_tokens(s, n);
     if (rc) return rc;
-    if (n) std::memcpy(s->h_tokens, tokens, sizeof(int32_t) * n);
+    if (s->staged_pending) {
+        Q38S_CUDA(cudaEventSynchronize(s->staged), "token upload");
+        s->staged_pending = false;
+    }
     s->h_offsets[0] = 0;
     s->h_offsets[1] = static_cast<uint32_t>(n);
-    if (n)
-        Q38S_CUDA(cudaMemcpyAsync(s->d_tokens, s->h_tokens, sizeof(int32_t) * n,
-                                  cudaMemcpyHostToDevice, s->stream),
-                  "token upload");
-    Q38S_CUDA(cudaMemcpyAsync(s->d_offsets, s->h_offsets, sizeof(uint32_t) * 2,
+    if (n) std::memcpy(s->h_tokens, tokens, sizeof(int32_t) * n);
+    Q38S_CUDA(cudaMemcpyAsync(s->d_stage, s->h_stage, sizeof(uint32_t) * (2 + n),
                               cudaMemcpyHostToDevice, s->stream),
               "token upload");
+    Q38S_CUDA(cudaEventRecord(s->staged, s->stream), "token upload");
+    s->staged_pending = true;
     return Q38S_OK;
 }
 
@@ -665,6 +665,8 @@ int prepare_common(const q38s_sampler* cs, const void* d_logits, uint16_t dtype,
     // read-back copy and no stream synchronisation on the common path.
     a.decisions = s->d_decision;
     a.decisions_host = 1;
+    a.rng_from_args = 1;  // the committed state lives on the host
+    a.rng_state = s->state.rng_state;
     if (n_extra) {
         a.extra_mode = 1;
         a.extra_tokens = s->d_tokens;
@@ -755,15 +757,9 @@ int q38s_sampler_commit(q38s_sampler* s, const q38s_decision_v1* d) {
         static_cast<uint32_t>(d->token) >= s->batch->vocab ||
         d->rng_before != s->state.rng_state || d->rng_after != d->rng_before + kGamma)
         return fail(Q38S_LOGIC_ERROR, kMsgMismatch);
+    // host only: prepare passes the committed rng state to the kernel
     s->state.rng_state = d->rng_after;
     ++s->state.sampled_tokens;
-    DeviceGuard g(s->batch->device);
-    RowState rs{s->state.rng_state, s->state.sampled_tokens, s->state.canonical_tokens,
-                s->state.penalty_checksum};
-    Q38S_CUDA(cudaMemcpyAsync(s->batch->d_state, &rs, sizeof(rs), cudaMemcpyHostToDevice,
-                              s->stream),
-              "commit");
-    Q38S_CUDA(cudaStreamSynchronize(s->stream), "commit");
     return ok();
 }
 
@@ -783,7 +779,7 @@ int q38s_sampler_commit_tokens(q38s_sampler* s, const int32_t* tokens, size_t co
                                            s->batch->vocab, 0, 1, s->d_tokens, s->d_offsets,
                                            nullptr, s->stream);
         if (e != cudaSuccess) return cuda_fail(static_cast<cudaError_t>(e), "commit_tokens");
-        Q38S_CUDA(cudaStreamSynchronize(s->stream), "commit_tokens");
+        // no synchronisation: later calls are ordered after it on s->stream
         for (size_t i = 0; i < valid; ++i) {
             ++s->state.canonical_tokens;
             s->state.penalty_checksum ^=
@@ -838,13 +834,9 @@ constexpr uint32_t kNoAllocBitmapWords = ((kNoAllocVocab + 127) / 128) * 4;
 struct NoAllocLayout {  // byte offsets into the static array
     static constexpr size_t params = 0;
     static constexpr size_t state = params + 256;
-    static constexpr size_t tickets = state + 256;
-    static constexpr size_t bitmap = tickets + 256;
-    static constexpr size_t seg_hdr =
-        bitmap + sizeof(uint32_t) * static_cast<size_t>(kNoAllocBitmapWords) * kNoAllocRows;  // zeros
-    static constexpr size_t seg_keys = seg_hdr + sizeof(uint32_t) * 4 * kMaxSegUnits;
+    static constexpr size_t bitmap = state + 256;  // zeros
     static constexpr size_t keys =
-        seg_keys + sizeof(uint64_t) * static_cast<size_t>(kMaxSegUnits) * kSegCap;
+        bitmap + sizeof(uint32_t) * static_cast<size_t>(kNoAllocBitmapWords) * kNoAllocRows;
     static constexpr size_t weights =
         keys + sizeof(uint32_t) * static_cast<size_t>(kNoAllocVocab) * kNoAllocRows;
     static constexpr size_t end =
@@ -860,7 +852,7 @@ std::mutex g_noalloc_mu;
 unsigned char* g_noalloc_ptr[64] = {};  // device address per device ordinal
 
 // Once per device, with that device current: the array's device address,
-// and the zero penalty bitmap / tickets the kernel expects.
+// and the zero penalty bitmap the kernel expects.
 int noalloc_setup(int device, unsigned char** out) {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     if (device < 0 || device >= 64) return fail(Q38S_CUDA_ERROR, "device ordinal out of range");
@@ -906,14 +898,13 @@ extern "C" int q38s_prepare_noalloc(const void* logits, uint16_t dtype, uint32_t
     int rc = noalloc_setup(device, &base);
     if (rc) return rc;
     auto s = static_cast<cudaStream_t>(stream);
-    // per-call inputs into the array; the tickets start at zero
+    // per-call inputs into the array
     Q38S_CUDA(cudaMemcpyAsync(base + NoAllocLayout::params, params, sizeof(RowParams) * rows,
                               cudaMemcpyHostToDevice, s),
               "no-alloc parameters");
     Q38S_CUDA(cudaMemcpyAsync(base + NoAllocLayout::state, states, sizeof(RowState) * rows,
                               cudaMemcpyHostToDevice, s),
               "no-alloc states");
-    Q38S_CUDA(cudaMemsetAsync(base + NoAllocLayout::tickets, 0, 256, s), "no-alloc tickets");
     const uint32_t es = dtype == Q38S_DTYPE_BF16 ? 2u : 4u;
     SampleArgs a;
     std::memset(&a, 0, sizeof(a));
@@ -937,9 +928,6 @@ extern "C" int q38s_prepare_noalloc(const void* logits, uint16_t dtype, uint32_t
     a.decisions = decisions;
     a.scratch = reinterpret_cast<uint32_t*>(base + NoAllocLayout::keys);
     a.scratch_w = reinterpret_cast<float*>(base + NoAllocLayout::weights);
-    a.seg_keys = reinterpret_cast<uint64_t*>(base + NoAllocLayout::seg_keys);
-    a.seg_hdr = reinterpret_cast<uint32_t*>(base + NoAllocLayout::seg_hdr);
-    a.row_ticket = reinterpret_cast<uint32_t*>(base + NoAllocLayout::tickets);
     a.segs = stream_segments(rows, vocabulary, device);
     const int e = launch_stream(a, stream);
     if (e != cudaSuccess) return cuda_fail(static_cast<cudaError_t>(e), "prepare_noalloc");

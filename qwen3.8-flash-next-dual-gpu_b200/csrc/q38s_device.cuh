@@ -160,6 +160,57 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase,
 // ~2 s at 1.9 GHz: far beyond any legitimate copy of a few tens of KB.
 constexpr long long kWaitLimitCycles = 4000000000ll;
 
+// ------------------------------------------- thread-block cluster (DSMEM)
+// The address of the same shared-memory location in CTA `rank` of this
+// CTA's cluster (its own rank included), for the shared::cluster forms.
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_u64(uint32_t addr, uint64_t v) {
+    asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_cluster_u64(uint32_t addr) {
+    uint64_t v;
+    asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
+    return v;
+}
+// Orders this thread's earlier accesses (and those it has synchronised
+// with) before its later ones for every thread of the cluster.
+__device__ __forceinline__ void fence_acq_rel_cluster() {
+    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+}
+// One arrival, release at cluster scope, on an mbarrier given by its
+// cluster address (another CTA's, or this CTA's own).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+                 : "memory");
+}
+// Bounded wait, acquire at cluster scope, on one of this CTA's mbarriers
+// that other CTAs of the cluster arrive on.  Returns true on completion.
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t phase,
+                                                          long long limit) {
+    const long long start = clock64();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n"
+            " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}" : "=r"(ok) : "r"(smem_addr(bar)), "r"(phase) : "memory");
+        if (ok) return true;
+        if (clock64() - start > limit) return false;
+    }
+}
+// Every thread of every CTA of the cluster (the whole block calls it).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n"
+                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // ------------------------------------------------------------ warp utils
 __device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
     for (int o = 16; o > 0; o >>= 1) {

@@ -57,6 +57,11 @@ struct SampleArgs {
     // the draw of virtual row v uses rng_state + (1 + rng_offset(v)) * gamma,
     // rng_offset(v) = rng_step ? (v < split ? v : v - split) : 0
     int rng_step;
+    // rng_from_args: the rng_state of every state row is rng_state below,
+    // not the state array's (the one-session sampler keeps its committed
+    // state on the host, so a commit needs no device update)
+    int rng_from_args;
+    uint64_t rng_state;
     // additional penalty tokens: 0 none; 1 CSR (extra_offsets); 2 prefix of
     // extra_tokens of length (v < split ? v : v - split)
     int extra_mode;
@@ -78,19 +83,14 @@ struct SampleArgs {
     const int32_t* draft_tokens;
     uint32_t* ticket;
     // streaming sampler (q38s_stream.cu): each virtual row is split into
-    // `segs` column segments; a row with segs > 1 parks each segment's
-    // sorted candidate list in seg_keys/seg_hdr (one slot per unit
-    // v * segs + s) and the last segment to finish (row_ticket[v]) merges
-    // them.  row_ticket words are zero between launches.
+    // `segs` column segments; with segs > 1 the kernel runs as clusters of
+    // segs CTAs, one cluster per row, and the segments' lists are merged
+    // in the cluster's shared memory
     uint32_t segs;
-    uint64_t* seg_keys;   // units * kSegCap rank keys
-    uint32_t* seg_hdr;    // units * 4 words: length, flags, max key, unused
-    uint32_t* row_ticket; // vrows words
 };
 
-// Streaming-sampler limits (q38s_stream.cu).
-constexpr uint32_t kSegCap = 512;       // candidates a segment hands to the merge
-constexpr uint32_t kMaxSegUnits = 512;  // vrows * segs when segs > 1
+// Most segments per row (the portable cluster size).
+constexpr uint32_t kMaxSegs = 8;
 
 // Launchers (q38s_stream.cu, q38s_sample.cu).  All return a cudaError_t as int.
 int launch_stream(const SampleArgs& a, void* stream);   // streaming sampler

@@ -56,7 +56,7 @@ constexpr uint32_t kRing = 4;                    // ring slots per CTA
 constexpr int kCons = 256;                       // consumer threads (warps 0-7)
 constexpr int kBlock = kCons + 32;               // + the producer warp
 constexpr uint32_t kBuf = 2048;                  // candidate buffer (rank keys)
-constexpr uint32_t kFinal = kSegCap;             // candidates entering the epilogue
+constexpr uint32_t kFinal = 512;                 // candidates entering the epilogue
 constexpr uint32_t kGather = 1024;               // exact gather of the general path
 constexpr uint32_t kArea = 32768;                // candidate / epilogue work area
 constexpr double kFix = 8796093022208.0;         // 2^43: fixed-point weight unit
@@ -69,8 +69,9 @@ static_assert(kBuf * 8 + kFinal * 8 + 3 * kFinal * 8 <= kArea, "fast-path area")
 
 // Optional per-unit trace (build with -DQ38S_TRACE; off in the product
 // build): 16 words per unit -- global-timer stamps of the unit's phases, its
-// threshold, candidate count, flags and the path that finished it.  The
-// buffer is installed with q38s_trace_install().
+// threshold, candidate count, flags and the path that finished it; the SM
+// clock at each stamp 131,072 words further.  The buffer is installed with
+// q38s_trace_install().
 #ifdef Q38S_TRACE
 __device__ unsigned long long* g_trace = nullptr;
 __device__ __forceinline__ unsigned long long gtime() {
@@ -84,7 +85,13 @@ __device__ __forceinline__ unsigned long long gtime() {
             g_trace[static_cast<size_t>(u) * 16 + (slot)] =                       \
                 static_cast<unsigned long long>(val);                             \
     } while (0)
-#define Q38S_TT(u, slot) Q38S_TR(u, slot, gtime())
+#define Q38S_TT(u, slot)                                                          \
+    do {                                                                          \
+        Q38S_TR(u, slot, gtime());                                                \
+        if (g_trace && threadIdx.x == 0 && (u) < 8192)                            \
+            g_trace[131072 + static_cast<size_t>(u) * 16 + (slot)] =              \
+                static_cast<unsigned long long>(clock64());                       \
+    } while (0)
 #else
 #define Q38S_TR(u, slot, val) do { } while (0)
 #define Q38S_TT(u, slot) do { } while (0)
@@ -113,6 +120,16 @@ struct __align__(16) Ctl {
     uint32_t e_r;
     double e_total;
     double e_draw;
+    // rows split over the CTAs of a cluster: the leader (rank 0) collects
+    // every segment's list header; each segment waits for the leader to
+    // have read its list before it reuses its shared memory
+    uint64_t xfull;                 // leader: all headers of the row arrived
+    uint64_t xdone;                 // member: the leader has read the list
+    uint64_t xh_top[kMaxSegs];      // leader: each list's first two entries
+    uint64_t xh_snd[kMaxSegs];
+    uint32_t xh_len[kMaxSegs];      // ... its length, flags, k-th value key
+    uint32_t xh_flags[kMaxSegs];
+    uint32_t xh_kth[kMaxSegs];
 };
 
 // ------------------------------------------------------ consumer barriers
@@ -221,6 +238,7 @@ __device__ void load_row(const SampleArgs& a, uint32_t v, Row& r) {
     r.p = a.params[r.srow];
     const uint32_t off = v < a.split ? v : v - a.split;
     r.st = a.state[r.srow];
+    if (a.rng_from_args) r.st.rng_state = a.rng_state;
     r.rng_before = r.st.rng_state + (a.rng_step ? static_cast<uint64_t>(off) * kGamma : 0ull);
     r.pen = (r.p.flags & kFlagPenalties) != 0;
     r.nonmono = (r.p.flags & kFlagNonMonotone) != 0;
@@ -810,23 +828,23 @@ __device__ void row_output(const SampleArgs& a, const Row& r, const uint64_t* so
 // kAcceptDomain), s_i = rng_state + (i + 1) * gamma; the first rejection
 // draws from max(0, p_i - q_i) over p_i's sorted support with
 // uniform01(s_i); if every draft is accepted the bonus token is the
-// reference draw from p_n.  The probability lookups run in parallel (four
-// threads per draft, then one thread per support entry); the ordered walk
-// over the drafts and the sequential sums of the residual draw run in one
-// thread, in the order written here.  Other CTAs wrote the arrays read
-// here: L2 loads.
+// reference draw from p_n.  The probability lookups and the per-draft
+// verdicts run in parallel (four threads per draft, then one thread per
+// draft or support entry); the first draft that is not accepted ends the
+// walk; the sequential sums of the residual draw run in one thread, in the
+// order written here.  Other CTAs wrote the arrays read here: L2 loads.
 __device__ void mtp_finish(const SampleArgs& a, unsigned char* area, Ctl& c) {
     const uint32_t n = a.n_draft;
     const uint32_t cap = a.dist.capacity;
     const uint32_t tid = threadIdx.x;
     const uint64_t rng0 = __ldcg(reinterpret_cast<const unsigned long long*>(
         &a.state[a.vrow_state_const].rng_state));
-    // phase-one layout of the area: result, per-draft p(d), q(d), flags, row headers
+    // phase-one layout of the area: result, per-draft p(d), q(d), row
+    // headers, verdicts
     q38s_mtp_result* rs = reinterpret_cast<q38s_mtp_result*>(area);
     double* pd = reinterpret_cast<double*>(area + 512);
     double* qd = pd + 64;
-    uint32_t* acc = reinterpret_cast<uint32_t*>(qd + 64);
-    int32_t* hs = reinterpret_cast<int32_t*>(acc + 64);  // row i: t_status, t_token, d_status, np, nq, d
+    int32_t* hs = reinterpret_cast<int32_t*>(qd + 64);  // row i: t_status, t_token, d_status, np, nq, d
     if (tid <= n) {
         int32_t* h = hs + tid * 6;
         h[0] = __ldcg(&a.decisions[tid].status);
@@ -865,51 +883,70 @@ __device__ void mtp_finish(const SampleArgs& a, unsigned char* area, Ctl& c) {
         }
     }
     cbar();
-    if (tid < n) {
-        const uint64_t s_i = rng0 + (static_cast<uint64_t>(tid) + 1) * kGamma;
-        acc[tid] = uniform01(s_i ^ kAcceptDomain) * qd[tid] < pd[tid] ? 1u : 0u;
+    // Each row's verdict, by the thread that loaded it, in the walk's order
+    // of checks: 0 draft accepted, 1 draft rejected, 2 the bonus row, 3 a
+    // row failed (its status in vs).  The walk stops at the first row whose
+    // verdict is not 0.
+    uint32_t* vd = reinterpret_cast<uint32_t*>(hs + 65 * 6);
+    int32_t* vs = reinterpret_cast<int32_t*>(vd + 65);
+    if (tid <= n) {
+        const int32_t* h = hs + tid * 6;
+        uint32_t v = 0;
+        int32_t st = Q38S_ROW_OK;
+        if (h[0] != Q38S_ROW_OK) {
+            v = 3;
+            st = h[0];
+        } else if (tid == n) {
+            v = 2;
+        } else if (h[2] != Q38S_ROW_OK) {
+            v = 3;
+            st = h[2];
+        } else if (static_cast<uint32_t>(h[3]) > cap || static_cast<uint32_t>(h[4]) > cap ||
+                   h[3] == 0) {
+            v = 3;
+            st = Q38S_ROW_NORMALIZATION;
+        } else {
+            const uint64_t s_i = rng0 + (static_cast<uint64_t>(tid) + 1) * kGamma;
+            v = uniform01(s_i ^ kAcceptDomain) * qd[tid] < pd[tid] ? 0u : 1u;
+        }
+        vd[tid] = v;
+        vs[tid] = st;
     }
     cbar();
-    // the drafts in order (one thread, shared memory only)
+    if (tid < 32) {
+        uint32_t first = n;  // the bonus row's verdict is never 0
+        for (uint32_t i0 = 0; i0 <= n; i0 += 32) {
+            const uint32_t i = i0 + tid;
+            const uint32_t b = __ballot_sync(0xffffffffu, i <= n && vd[i] != 0u);
+            if (b) {
+                first = i0 + __ffs(b) - 1;
+                break;
+            }
+        }
+        if (tid == 0) c.bc_u32[0] = first;
+    }
+    cbar();
+    const uint32_t first = c.bc_u32[0];
+    if (tid < first) rs->tokens[tid] = hs[tid * 6 + 5];  // the accepted drafts
+    cbar();
     if (tid == 0) {
         rs->rng_before = rng0;
         rs->status = Q38S_ROW_OK;
-        rs->n_tokens = 0;
-        rs->n_accepted = 0;
+        rs->n_accepted = first;
+        rs->n_tokens = first;
         uint32_t rej = 0xffffffffu;
-        for (uint32_t i = 0; i <= n; ++i) {
-            const int32_t* h = hs + i * 6;
-            if (h[0] != Q38S_ROW_OK) {
-                rs->status = h[0];
-                break;
-            }
-            if (i == n) {  // bonus row: the reference draw from p_n
-                rs->tokens[rs->n_tokens++] = h[1];
-                break;
-            }
-            if (h[2] != Q38S_ROW_OK) {
-                rs->status = h[2];
-                break;
-            }
-            const uint32_t np = static_cast<uint32_t>(h[3]), nq = static_cast<uint32_t>(h[4]);
-            if (np > cap || nq > cap || np == 0) {
-                rs->status = Q38S_ROW_NORMALIZATION;
-                break;
-            }
-            if (acc[i]) {
-                rs->tokens[rs->n_tokens++] = h[5];
-                ++rs->n_accepted;
-                continue;
-            }
-            rej = i;
-            break;
-        }
-        c.bc_u32[0] = rej;
-        if (rej != 0xffffffffu) {
+        if (vd[first] == 3) {
+            rs->status = vs[first];
+        } else if (vd[first] == 2) {  // bonus row: the reference draw from p_n
+            rs->tokens[first] = hs[first * 6 + 1];
+            rs->n_tokens = first + 1;
+        } else {
+            rej = first;
             c.bc_u32[1] = static_cast<uint32_t>(hs[rej * 6 + 3]);
             c.bc_u32[2] = static_cast<uint32_t>(hs[rej * 6 + 4]);
             c.bc_u32[3] = static_cast<uint32_t>(hs[rej * 6 + 1]);
         }
+        c.bc_u32[0] = rej;
     }
     cbar();
     const uint32_t rej = c.bc_u32[0];
@@ -974,8 +1011,9 @@ __device__ void row_done(const SampleArgs& a, unsigned char* area, Ctl& c) {
     if (!a.mtp) return;
     cbar();
     // one GPU-scope acquire-release ticket (see the segment merge)
-    if (threadIdx.x == 0)
+    if (threadIdx.x == 0) {
         c.bc_u32[2] = atom_add_acq_rel_gpu(a.ticket, 1u) == a.vrows - 1;
+    }
     cbar();
     if (c.bc_u32[2]) {
         if (threadIdx.x == 0) *a.ticket = 0;
@@ -1426,6 +1464,8 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             mbar_init(&c.full[i], 1);
             mbar_init(&c.empty[i], kCons / 32);  // one arrival per consumer warp
         }
+        mbar_init(&c.xfull, a.segs);  // one arrival per segment of a row
+        mbar_init(&c.xdone, 1);       // the leader's
         c.abort_flag = 0;
         c.prod_done = 0;
         c.issued = 0;
@@ -1433,6 +1473,9 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
         fence_mbar_init();
     }
     __syncthreads();
+    // a row split into segments runs on one cluster: no CTA arrives on a
+    // peer's barriers before the peer has initialised them
+    if (a.segs > 1) cluster_sync_all();
     if (tid >= static_cast<uint32_t>(kCons)) {
         if (tid == static_cast<uint32_t>(kCons)) produce<DT>(a, ring, c);
         return;
@@ -1455,6 +1498,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
     const uint32_t S = a.segs;
     const uint32_t n_units = a.vrows * S;
     uint32_t g = 0;     // tiles passed (the producer's order)
+    uint32_t xrow = 0;  // multi-segment rows passed (the cluster barriers' parity)
     bool stop = false;  // this warp gave up on a copy (warp-uniform)
     (void)warp;
     for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
@@ -1779,88 +1823,68 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             cbar();
             continue;
         }
-        // ---- multi-segment row: park the list, the last segment merges
+        // ---- multi-segment row: the S CTAs of a cluster hold its segments
+        // (cluster rank = segment).  Each keeps its sorted list in its own
+        // shared memory and hands the list's header to the leader (rank 0)
+        // through distributed shared memory; the leader reads the entries
+        // that can still qualify straight from the segments' shared memory,
+        // then lets each segment go on.
         {
-            const size_t base = static_cast<size_t>(u) * kSegCap;
             const uint32_t len = (flags & (kFTimeout | kFInf | kFOverflow)) ? 0u : keep;
-            for (uint32_t i = tid; i < len; i += kCons) a.seg_keys[base + i] = sorted[i];
+            const uint32_t par = xrow & 1u;
+            ++xrow;
+            cbar();  // the list is complete
             if (tid == 0) {
-                a.seg_hdr[u * 4 + 0] = len;
-                a.seg_hdr[u * 4 + 1] = flags;
+                const uint64_t top = len > 0 ? sorted[0] : 0ull;
+                const uint64_t snd = len > 1 ? sorted[1] : 0ull;
+                const uint32_t kth = (r.k_eff && len >= r.k_eff)
+                    ? static_cast<uint32_t>(sorted[r.k_eff - 1] >> 32) : 0u;
+                st_cluster_u32(cluster_addr(&c.xh_len[seg], 0), len);
+                st_cluster_u32(cluster_addr(&c.xh_flags[seg], 0), flags);
+                st_cluster_u32(cluster_addr(&c.xh_kth[seg], 0), kth);
+                st_cluster_u64(cluster_addr(&c.xh_top[seg], 0), top);
+                st_cluster_u64(cluster_addr(&c.xh_snd[seg], 0), snd);
+                // the list (every thread's writes, ordered by the barrier
+                // that ended finish_buffer) and the header before the arrival
+                fence_acq_rel_cluster();
+                mbar_arrive_cluster(cluster_addr(&c.xfull, 0));
             }
-            cbar();
-            // one GPU-scope acquire-release ticket: it publishes the CTA's
-            // writes above (ordered before it by the barrier) and, for the
-            // last segment, makes every other segment's writes visible
-            if (tid == 0) c.bc_u32[2] = atom_add_acq_rel_gpu(&a.row_ticket[v], 1u) == S - 1;
-            cbar();
-            if (!c.bc_u32[2]) {
+            if (seg != 0) {
+                // the list stays put until the leader has read it (a wait
+                // that runs out leaves the row to the leader's status)
+                if (tid == 0) mbar_wait_cluster_bounded(&c.xdone, par, kWaitLimitCycles);
+                cbar();
                 Q38S_TR(u, 8, 3);
                 Q38S_TT(u, 9);
                 continue;
             }
-            // Segment headers in parallel (thread s reads segment s's length,
-            // flags, largest entry and k-th entry).  The lists are sorted, so
-            // the row's k-th largest value is at least every segment's k-th,
-            // and the row's largest value is the largest first entry: only
-            // entries at or above the better of that bound and the min-p
-            // bound need to be merged.
-            uint32_t my_len = 0, my_flags = 0, my_kth = 0, my_top = 0, my_2nd = 0;
-            uint64_t top64 = 0, snd64 = 0;  // the segment's first two entries
-            if (tid < S) {
-                const uint64_t* src = a.seg_keys + static_cast<size_t>(v * S + tid) * kSegCap;
-                my_len = __ldcg(&a.seg_hdr[(v * S + tid) * 4 + 0]);
-                my_flags = __ldcg(&a.seg_hdr[(v * S + tid) * 4 + 1]);
-                const uint64_t top = __ldcg(reinterpret_cast<const unsigned long long*>(src));
-                const uint64_t snd = __ldcg(reinterpret_cast<const unsigned long long*>(src + 1));
-                const uint64_t kth = (r.k_eff && r.k_eff <= kSegCap)
-                    ? __ldcg(reinterpret_cast<const unsigned long long*>(src + r.k_eff - 1)) : 0ull;
-                if (my_len) my_top = static_cast<uint32_t>(top >> 32);
-                if (my_len > 1) my_2nd = static_cast<uint32_t>(snd >> 32);
-                top64 = top;
-                snd64 = snd;
-                if (r.k_eff && my_len >= r.k_eff) my_kth = static_cast<uint32_t>(kth >> 32);
-            }
+            if (tid == 0) c.bc_u32[2] = mbar_wait_cluster_bounded(&c.xfull, par, kWaitLimitCycles);
             if (tid == 0) c.n_cand = 0;
-            Q38S_TT(u, 13);
-            if (tid < S) {
-                c.hist[64 + tid] = my_flags;
-                c.hist[128 + tid] = my_kth;
-                c.hist[192 + tid] = my_top;
-            }
             cbar();
-            Q38S_TT(u, 15);
-            uint32_t rflags = 0, mkth = 0, mtop = 0;
-#pragma unroll 4
+            Q38S_TT(u, 13);
+            uint32_t rflags = c.bc_u32[2] ? 0u : kFTimeout;
+            uint32_t mkth = 0, mtop = 0;
             for (uint32_t s2 = 0; s2 < S; ++s2) {
-                rflags |= c.hist[64 + s2];
-                mkth = max(mkth, c.hist[128 + s2]);
-                mtop = max(mtop, c.hist[192 + s2]);
+                rflags |= c.xh_flags[s2];
+                mkth = max(mkth, c.xh_kth[s2]);
+                if (c.xh_len[s2]) mtop = max(mtop, static_cast<uint32_t>(c.xh_top[s2] >> 32));
             }
-            // the k-th largest of the segments' two first entries (distinct
-            // entries of the union) bounds the row's k-th largest too
+            // The lists are sorted: the row's k-th largest value is at least
+            // every segment's k-th and the k-th largest of the segments' two
+            // first entries (distinct entries of the row); its largest value
+            // is the largest first entry.  Only entries at or above the
+            // better bound (and the min-p bound) are merged.
             if (r.k_eff && r.k_eff <= 2 * S) {
-                cbar();
-                if (tid < S) {
-                    c.tkey[2 * tid] = my_top;
-                    c.tkey[2 * tid + 1] = my_2nd;
-                }
-                cbar();
                 if (warp == 0) {
-                    uint32_t kk[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint32_t j = lane + 32u * i;
-                        kk[i] = j < 2 * S ? c.tkey[j] : 0u;
-                    }
+                    const uint32_t s2 = lane >> 1;
+                    uint32_t kk = 0;
+                    if (s2 < S && c.xh_len[s2] > (lane & 1u))
+                        kk = static_cast<uint32_t>(((lane & 1u) ? c.xh_snd[s2] : c.xh_top[s2]) >> 32);
                     uint32_t tt = 0;
 #pragma unroll 1
                     for (int b = 31; b >= 16; --b) {
-                        const uint32_t cand = tt | (1u << b);
-                        uint32_t cnt = 0;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) cnt += kk[i] >= cand ? 1u : 0u;
-                        if (__reduce_add_sync(kFull, cnt) >= r.k_eff) tt = cand;
+                        const uint32_t cand_b = tt | (1u << b);
+                        if (__popc(__ballot_sync(kFull, kk >= cand_b)) >= r.k_eff) tt = cand_b;
                     }
                     if (lane == 0) c.bc_u32[0] = tt;
                 }
@@ -1869,61 +1893,36 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             }
             if (a.mode == kModeShardTopK) rflags &= ~kFInf;
             uint32_t rkeep = 0;
+            bool over = false;
             if (!(rflags & (kFTimeout | kFInf | kFOverflow))) {
                 uint32_t th = mkth;
                 if (r.minp) th = max(th, minp_key(mtop, r));
-                // Entries at or above th.  The lists are sorted: a segment whose
-                // second entry is below th contributes at most its first (both
-                // are in registers); the rest of the others' lists are read in
-                // one flattened pass (a handful per thread, all in flight).
-                bool over = false;
-                over |= warp_push(tid < S && my_len > 0 && my_top >= th, top64, cand, kBuf, &c.n_cand);
-                over |= warp_push(tid < S && my_len > 1 && my_2nd >= th, snd64, cand, kBuf, &c.n_cand);
-                const uint32_t rem = (tid < S && my_len > 2 && my_2nd >= th) ? my_len - 2 : 0u;
-                uint32_t n_rem;
-                const uint32_t rem_off = cscan_excl(rem, &n_rem, c);
-                if (n_rem) {
-                    if (tid < S) c.hist[tid] = rem_off;
-                    cbar();
-                    constexpr int kPer = kBuf / kCons;
-                    uint64_t e[kPer];
-#pragma unroll
-                    for (int j = 0; j < kPer; ++j) {
-                        const uint32_t idx = tid + j * kCons;
-                        e[j] = 0ull;
-                        if (idx < n_rem && idx < kBuf) {
-                            uint32_t lo = 0, hi = S - 1;  // last segment starting at or before idx
-                            while (lo < hi) {
-                                const uint32_t mid = (lo + hi + 1) / 2;
-                                if (c.hist[mid] <= idx) lo = mid;
-                                else hi = mid - 1;
-                            }
-                            e[j] = __ldcg(reinterpret_cast<const unsigned long long*>(
-                                a.seg_keys + static_cast<size_t>(v * S + lo) * kSegCap + 2 +
-                                (idx - c.hist[lo])));
-                        }
-                    }
-                    over |= n_rem > kBuf;
-#pragma unroll
-                    for (int j = 0; j < kPer; ++j) {
-                        const uint32_t idx = tid + j * kCons;
-                        const bool keep = idx < n_rem && idx < kBuf &&
-                                          static_cast<uint32_t>(e[j] >> 32) >= th;
-                        over |= warp_push(keep, e[j], cand, kBuf, &c.n_cand);
+                // warp w reads segment w's list down to the first entry below th
+                if (warp < S) {
+                    const uint32_t ls = c.xh_len[warp];
+                    const uint32_t src = cluster_addr(sorted, warp);
+                    for (uint32_t i0 = 0; i0 < ls; i0 += 32) {
+                        const uint32_t i = i0 + lane;
+                        const uint64_t e = i < ls ? ld_cluster_u64(src + 8u * i) : 0ull;
+                        const bool in = i < ls && static_cast<uint32_t>(e >> 32) >= th;
+                        over |= warp_push(in, e, cand, kBuf, &c.n_cand);
+                        if (__ballot_sync(kFull, i < ls && !in)) break;
                     }
                 }
-                over = cbar_or(over);
-                Q38S_TT(u, 6);
+            }
+            over = cbar_or(over);  // also: every read of the segments' lists is done
+            if (tid > 0 && tid < S) mbar_arrive_cluster(cluster_addr(&c.xdone, tid));
+            Q38S_TT(u, 6);
+            if (!(rflags & (kFTimeout | kFInf | kFOverflow))) {
                 const uint32_t nm = min(c.n_cand, kBuf);
                 if (over) rflags |= kFOverflow;  // more than the buffer holds
                 if (!(rflags & kFOverflow)) {
                     rkeep = finish_buffer(cand, nm, r, sorted, c, true);
                     if (rkeep == 0xffffffffu) rflags |= kFOverflow;
                 }
-                Q38S_TT(u, 10);
                 Q38S_TR(u, 14, nm);
             }
-            if (tid == 0) a.row_ticket[v] = 0;  // every segment has arrived: reset for the next call
+            Q38S_TT(u, 10);
             Q38S_TR(u, 8, 4 + ((rflags & kFOverflow) ? 1 : 0));
             finish_row<DT>(a, r, rflags, sorted, rkeep, area, c);
             Q38S_TT(u, 9);
@@ -1976,8 +1975,7 @@ uint32_t stream_segments(uint32_t vrows, uint32_t vocab, int device) {
     const uint32_t nblk = (vocab + 127) / 128;
     const uint32_t by_cols = nblk / 16;  // segments of at least 2,048 columns
     if (s > by_cols) s = by_cols;
-    if (s > 64) s = 64;
-    while (s > 1 && vrows * s > kMaxSegUnits) --s;
+    if (s > kMaxSegs) s = kMaxSegs;
     return s < 1 ? 1 : s;
 }
 
@@ -2005,9 +2003,26 @@ static int launch_stream_t(const SampleArgs& a, void* stream) {
 #ifdef Q38S_TRACE
     if (const char* gc = getenv("Q38S_TRACE_GRID")) cap = static_cast<uint32_t>(atoi(gc));
 #endif
+    cap -= cap % a.segs;  // whole clusters (units is a multiple of segs)
     const uint32_t grid = units < cap ? units : cap;
-    kern<<<grid, kBlock, smem, static_cast<cudaStream_t>(stream)>>>(a);
-    return cudaGetLastError();
+    if (a.segs == 1) {
+        kern<<<grid, kBlock, smem, static_cast<cudaStream_t>(stream)>>>(a);
+        return cudaGetLastError();
+    }
+    // one cluster of segs CTAs per row: CTA rank = segment
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kBlock);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.segs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
 }
 
 int launch_stream(const SampleArgs& a, void* stream) {

@@ -179,13 +179,18 @@ def _stream_ptr(stream):
     return C.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
 
 
+_DTYPES = None
+
+
 def _dtype_code(t) -> int:
-    import torch
-    if t.dtype == torch.bfloat16:
-        return DTYPE_BF16
-    if t.dtype == torch.float32:
-        return DTYPE_F32
-    raise TypeError("logits must be torch.bfloat16 or torch.float32")
+    global _DTYPES
+    if _DTYPES is None:
+        import torch
+        _DTYPES = {torch.bfloat16: DTYPE_BF16, torch.float32: DTYPE_F32}
+    code = _DTYPES.get(t.dtype)
+    if code is None:
+        raise TypeError("logits must be torch.bfloat16 or torch.float32")
+    return code
 
 
 class Sampler:
@@ -201,6 +206,14 @@ class Sampler:
         self._h = h
         self.vocabulary = vocabulary
         self.device = device
+        # reused per call: the decision out-parameter, a one-token buffer
+        self._dec = Decision()
+        self._dec_ref = C.byref(self._dec)
+        self._tok = (C.c_int32 * 1)()
+        self._tok_ref = C.cast(self._tok, C.c_void_p)
+        self._prepare_device = L.q38s_sampler_prepare_device
+        self._commit = L.q38s_sampler_commit
+        self._commit_tokens = L.q38s_sampler_commit_tokens
 
     def close(self):
         if getattr(self, "_h", None):
@@ -219,23 +232,36 @@ class Sampler:
         return d.token, d.rng_before, d.rng_after
 
     def prepare_device(self, logits, extra=(), stream=None) -> tuple[int, int, int]:
-        e = np.ascontiguousarray(np.asarray(extra, dtype=np.int32))
-        d = Decision()
-        _check(lib().q38s_sampler_prepare_device(
-            self._h, C.c_void_p(logits.data_ptr()), _dtype_code(logits), logits.numel(),
-            C.c_void_p(e.ctypes.data), e.size, C.byref(d), _stream_ptr(stream)))
+        # the per-token call: argument conversion kept to a minimum
+        if len(extra):
+            e = np.ascontiguousarray(np.asarray(extra, dtype=np.int32))
+            ep, en = e.ctypes.data, e.size
+        else:
+            ep, en = None, 0
+        d = self._dec
+        rc = self._prepare_device(self._h, logits.data_ptr(), _dtype_code(logits),
+                                  logits.numel(), ep, en, self._dec_ref,
+                                  None if stream is None else _stream_ptr(stream))
+        if rc:
+            _check(rc)
         return d.token, d.rng_before, d.rng_after
 
     def commit(self, decision) -> None:
-        d = Decision(decision[0], 0, decision[1], decision[2])
-        _check(lib().q38s_sampler_commit(self._h, C.byref(d)))
+        d = self._dec
+        d.token, d.status, d.rng_before, d.rng_after = decision[0], 0, decision[1], decision[2]
+        rc = self._commit(self._h, self._dec_ref)
+        if rc:
+            _check(rc)
 
     def commit_tokens(self, tokens) -> None:
         t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
         _check(lib().q38s_sampler_commit_tokens(self._h, C.c_void_p(t.ctypes.data), t.size))
 
     def commit_token(self, token: int) -> None:
-        self.commit_tokens([token])
+        self._tok[0] = token
+        rc = self._commit_tokens(self._h, self._tok_ref, 1)
+        if rc:
+            _check(rc)
 
     def reset(self) -> None:
         _check(lib().q38s_sampler_reset(self._h))
