@@ -171,9 +171,6 @@ __device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
 __device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
-__device__ __forceinline__ void st_cluster_u64(uint32_t addr, uint64_t v) {
-    asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
-}
 __device__ __forceinline__ uint64_t ld_cluster_u64(uint32_t addr) {
     uint64_t v;
     asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");

@@ -61,6 +61,8 @@ constexpr uint32_t kGather = 1024;               // exact gather of the general 
 constexpr uint32_t kArea = 32768;                // candidate / epilogue work area
 constexpr double kFix = 8796093022208.0;         // 2^43: fixed-point weight unit
 
+constexpr uint32_t kHdrKeys = 64;                // value keys per row in the segments' headers
+
 constexpr uint32_t kFOverflow = 1u;
 constexpr uint32_t kFInf = 2u;
 constexpr uint32_t kFTimeout = 4u;
@@ -73,7 +75,7 @@ static_assert(kBuf * 8 + kFinal * 8 + 3 * kFinal * 8 <= kArea, "fast-path area")
 // clock at each stamp 131,072 words further.  The buffer is installed with
 // q38s_trace_install().
 #ifdef Q38S_TRACE
-__device__ unsigned long long* g_trace = nullptr;
+__constant__ unsigned long long* g_trace = nullptr;  // constant: no reload per stamp
 __device__ __forceinline__ unsigned long long gtime() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -125,11 +127,10 @@ struct __align__(16) Ctl {
     // have read its list before it reuses its shared memory
     uint64_t xfull;                 // leader: all headers of the row arrived
     uint64_t xdone;                 // member: the leader has read the list
-    uint64_t xh_top[kMaxSegs];      // leader: each list's first two entries
-    uint64_t xh_snd[kMaxSegs];
-    uint32_t xh_len[kMaxSegs];      // ... its length, flags, k-th value key
+    uint32_t xh_len[kMaxSegs];      // leader: each list's length, flags, k-th value key
     uint32_t xh_flags[kMaxSegs];
     uint32_t xh_kth[kMaxSegs];
+    uint32_t xh_keys[kHdrKeys];     // ... and its first kHdrKeys / S value keys
 };
 
 // ------------------------------------------------------ consumer barriers
@@ -1464,7 +1465,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             mbar_init(&c.full[i], 1);
             mbar_init(&c.empty[i], kCons / 32);  // one arrival per consumer warp
         }
-        mbar_init(&c.xfull, a.segs);  // one arrival per segment of a row
+        mbar_init(&c.xfull, kHdrKeys / a.segs * a.segs);  // one per header key of a row
         mbar_init(&c.xdone, 1);       // the leader's
         c.abort_flag = 0;
         c.prod_done = 0;
@@ -1727,20 +1728,33 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                 hlist[hoff++] = static_cast<uint16_t>(t * kCons + tid);
             }
             cbar();
+            // the CTA's last unit of at most kRing tiles is still whole in
+            // the ring (tile t in slot (g - ntiles + t) % kRing, padded to
+            // whole vectors with -inf, its bitmap slice behind it): read it
+            // there instead of from L2
+            const bool resident = ntiles <= kRing && u + gridDim.x >= n_units;
 #pragma unroll 1
             for (uint32_t hi = tid; hi < n_hit; hi += kCons) {
                 const uint32_t t = hlist[hi] / kCons, thr = hlist[hi] % kCons;
                 const uint32_t t0 = c0 + t * TC;
                 const uint32_t n = min(c1 - t0, TC);
+                const unsigned char* sl = ring + ((g - ntiles + t) % kRing) * kSlot;
                 uint4 w[kU];
                 uint32_t pw[kU];
 #pragma unroll
                 for (int q = 0; q < kU; ++q) {  // every load in flight at once
                     const uint32_t e0 = (thr + q * kCons) * pv;
                     const uint32_t nv = e0 < n ? min(pv, n - e0) : 0u;
-                    w[q] = nv ? load_vec<DT>(a, src_row, t0 + e0, nv)
-                              : make_uint4(0u, 0u, 0u, 0u);
-                    pw[q] = (nv && r.pen) ? __ldg(&r.gbm[(t0 + e0) >> 5]) : 0u;
+                    if (resident) {
+                        w[q] = nv ? *reinterpret_cast<const uint4*>(sl + e0 * es)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+                        pw[q] = (nv && r.pen)
+                            ? reinterpret_cast<const uint32_t*>(sl + kTileBytes)[e0 >> 5] : 0u;
+                    } else {
+                        w[q] = nv ? load_vec<DT>(a, src_row, t0 + e0, nv)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+                        pw[q] = (nv && r.pen) ? __ldg(&r.gbm[(t0 + e0) >> 5]) : 0u;
+                    }
                 }
                 uint32_t cm = 0;  // bit q * pv + e: element e of vector q reaches rho
 #pragma unroll
@@ -1834,18 +1848,22 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             const uint32_t par = xrow & 1u;
             ++xrow;
             cbar();  // the list is complete
-            if (tid == 0) {
-                const uint64_t top = len > 0 ? sorted[0] : 0ull;
-                const uint64_t snd = len > 1 ? sorted[1] : 0ull;
-                const uint32_t kth = (r.k_eff && len >= r.k_eff)
-                    ? static_cast<uint32_t>(sorted[r.k_eff - 1] >> 32) : 0u;
-                st_cluster_u32(cluster_addr(&c.xh_len[seg], 0), len);
-                st_cluster_u32(cluster_addr(&c.xh_flags[seg], 0), flags);
-                st_cluster_u32(cluster_addr(&c.xh_kth[seg], 0), kth);
-                st_cluster_u64(cluster_addr(&c.xh_top[seg], 0), top);
-                st_cluster_u64(cluster_addr(&c.xh_snd[seg], 0), snd);
+            // lane j < m of warp 0 writes key j of the header (lane 0 also
+            // its length, flags and k-th key), then arrives on the leader's
+            // barrier itself: the leader waits for S * m arrivals
+            const uint32_t m = kHdrKeys / S;  // 8..32
+            if (tid < m) {
+                if (tid == 0) {
+                    const uint32_t kth = (r.k_eff && len >= r.k_eff)
+                        ? static_cast<uint32_t>(sorted[r.k_eff - 1] >> 32) : 0u;
+                    st_cluster_u32(cluster_addr(&c.xh_len[seg], 0), len);
+                    st_cluster_u32(cluster_addr(&c.xh_flags[seg], 0), flags);
+                    st_cluster_u32(cluster_addr(&c.xh_kth[seg], 0), kth);
+                }
+                st_cluster_u32(cluster_addr(&c.xh_keys[seg * m + tid], 0),
+                               tid < len ? static_cast<uint32_t>(sorted[tid] >> 32) : 0u);
                 // the list (every thread's writes, ordered by the barrier
-                // that ended finish_buffer) and the header before the arrival
+                // above) and this lane's header words before its arrival
                 fence_acq_rel_cluster();
                 mbar_arrive_cluster(cluster_addr(&c.xfull, 0));
             }
@@ -1867,30 +1885,33 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             for (uint32_t s2 = 0; s2 < S; ++s2) {
                 rflags |= c.xh_flags[s2];
                 mkth = max(mkth, c.xh_kth[s2]);
-                if (c.xh_len[s2]) mtop = max(mtop, static_cast<uint32_t>(c.xh_top[s2] >> 32));
+                if (c.xh_len[s2]) mtop = max(mtop, c.xh_keys[s2 * m]);
             }
             // The lists are sorted: the row's k-th largest value is at least
-            // every segment's k-th and the k-th largest of the segments' two
-            // first entries (distinct entries of the row); its largest value
-            // is the largest first entry.  Only entries at or above the
-            // better bound (and the min-p bound) are merged.
-            if (r.k_eff && r.k_eff <= 2 * S) {
-                if (warp == 0) {
-                    const uint32_t s2 = lane >> 1;
-                    uint32_t kk = 0;
-                    if (s2 < S && c.xh_len[s2] > (lane & 1u))
-                        kk = static_cast<uint32_t>(((lane & 1u) ? c.xh_snd[s2] : c.xh_top[s2]) >> 32);
-                    uint32_t tt = 0;
-#pragma unroll 1
-                    for (int b = 31; b >= 16; --b) {
-                        const uint32_t cand_b = tt | (1u << b);
-                        if (__popc(__ballot_sync(kFull, kk >= cand_b)) >= r.k_eff) tt = cand_b;
+            // every segment's k-th and the k-th largest of the segments'
+            // first m entries (distinct entries of the row); its largest
+            // value is the largest first entry.  Only entries at or above
+            // the better bound (and the min-p bound) are merged.
+            if (r.k_eff && r.k_eff <= S * m) {
+                // key x is the k-th largest when fewer than k keys exceed it
+                // and at least k reach it (every thread of warps 0-1 ranks one)
+                if (tid == 0) c.bc_u32[0] = 0;
+                cbar();
+                if (tid < S * m) {
+                    const uint32_t x = c.xh_keys[tid];
+                    uint32_t gt = 0, ge = 0;
+#pragma unroll 8
+                    for (uint32_t j = 0; j < S * m; ++j) {
+                        const uint32_t y = c.xh_keys[j];
+                        gt += y > x ? 1u : 0u;
+                        ge += y >= x ? 1u : 0u;
                     }
-                    if (lane == 0) c.bc_u32[0] = tt;
+                    if (x && gt < r.k_eff && ge >= r.k_eff) c.bc_u32[0] = x;  // equal writers
                 }
                 cbar();
                 mkth = max(mkth, c.bc_u32[0]);
             }
+            Q38S_TT(u, 15);
             if (a.mode == kModeShardTopK) rflags &= ~kFInf;
             uint32_t rkeep = 0;
             bool over = false;
