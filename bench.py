@@ -340,6 +340,23 @@ def batch1_latency(dev, stream):
         s.commit_token(d[0])
     lat.sort()
     rank = lambda q: lat[max(0, int(np.ceil(n_steps * q / 100.0)) - 1)]  # executor.cc:126-131
+    # the same loop driven from C++ through q38::TransactionalSampler (the
+    # reference executor's caller), lib/libq38s_latency.so
+    import ctypes as C
+    native = C.CDLL(os.path.join(os.path.dirname(q38s.LIB_PATH), "libq38s_latency.so"))
+    native.q38s_latency_batch1.argtypes = [C.c_uint32, C.c_void_p, C.c_void_p, C.c_size_t,
+                                           C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32,
+                                           C.c_void_p]
+    cfg1 = q38s.config_v1(top_k=c2["top_k"], top_p=c2["top_p"], temperature=c2["temperature"],
+                          presence_penalty=c2["presence_penalty"], seed=c2["seed"])
+    hist = np.ascontiguousarray(synth.cfg2_history(), dtype=np.int32)
+    nlat = np.empty(n_steps)
+    rc = native.q38s_latency_batch1(VOCAB, C.byref(cfg1), hist.ctypes.data, hist.size,
+                                    pool.data_ptr(), pool_n, 50, n_steps, nlat.ctypes.data)
+    if rc != 0:
+        raise RuntimeError(f"native batch-1 latency harness failed ({rc})")
+    nlat.sort()
+    nrank = lambda q: nlat[max(0, int(np.ceil(n_steps * q / 100.0)) - 1)]
     # device time of the same kernel, batch of 1 row, events over 2,000 calls
     b1 = q38s.Batch(VOCAB, [cfg], device=dev.index)
     b1.commit_tokens([synth.cfg2_history()])
@@ -351,11 +368,16 @@ def batch1_latency(dev, stream):
     dev_ms = time_steps(fns, 2000, stream) / 2000
     out["batch1"] = {"config": "cfg2: 1 row bf16, T 0.6, top_k 20, top_p 0.95, min_p 0, "
                                "presence 0.5, history 8,192 -> 18,192, 10,000 calls",
-                     "p50_us": float(rank(50)), "p99_us": float(rank(99)),
-                     "mean_us": float(lat.mean()), "device_us": dev_ms * 1e3,
-                     "call": "q38s_sampler_prepare_device (host wall time per call, incl. "
-                             "launch and the wait for the 24-byte decision, which the kernel "
-                             "writes into mapped host memory)",
+                     "p50_us": float(nrank(50)), "p99_us": float(nrank(99)),
+                     "mean_us": float(nlat.mean()),
+                     "call": "q38::TransactionalSampler::prepare_device from C++ (host wall "
+                             "time per call, incl. launch and the wait for the 24-byte "
+                             "decision, which the kernel writes into mapped host memory); "
+                             "commit + commit_token between calls",
+                     "python": {"p50_us": float(rank(50)), "p99_us": float(rank(99)),
+                                "mean_us": float(lat.mean()),
+                                "call": "q38s.Sampler.prepare_device (ctypes), same loop"},
+                     "device_us": dev_ms * 1e3,
                      "target_us": 20.0}
     return out
 

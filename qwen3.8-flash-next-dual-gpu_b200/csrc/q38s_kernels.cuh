@@ -89,7 +89,8 @@ struct SampleArgs {
     uint32_t segs;
 };
 
-// Most segments per row (the portable cluster size).
+// Most segments per row: one cluster per split row (8 is the portable
+// cluster size; above it the kernel allows non-portable sizes).
 constexpr uint32_t kMaxSegs = 8;
 
 // Launchers (q38s_stream.cu, q38s_sample.cu).  All return a cudaError_t as int.

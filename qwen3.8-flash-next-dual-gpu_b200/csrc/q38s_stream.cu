@@ -7,9 +7,10 @@
 // grid of at most two CTAs per SM walks the units (CTA b takes units b,
 // b + G, b + 2G, ...).  Large batches use one segment per row, so every row
 // is streamed start to finish by one CTA; small batches split rows so the
-// whole GPU pulls HBM.  The last segment of a row to finish (a ticket per
-// row, reset by that CTA) merges the segments' candidate lists.  No CTA ever
-// waits for another.
+// whole GPU pulls HBM.  A split row runs on one thread-block cluster (CTA
+// rank = segment): the segments' candidate lists stay in their CTAs' shared
+// memory and the leader (rank 0) merges them through distributed shared
+// memory.  CTAs of different clusters never wait for one another.
 //
 // Inside a CTA.  Warp 8 is a producer: one lane streams the CTA's tiles
 // (16 KB of logits each, plus the matching 1 KB slice of the row's penalty
@@ -20,17 +21,18 @@
 // the next unit) stay in flight while the consumers do per-row serial work.
 //
 // Per unit the consumers
-//   seed    take each thread's largest raw logit of the first tile, evaluate
-//           it exactly, and derive theta: the k-th largest of those 256
-//           values (a lower bound of the row's k-th largest value) and, for
-//           min-p rows, M + ln(min_p) - slack (M = the largest exact value
-//           seen, a lower bound of the row maximum);
-//   filter  one packed bf16x2 (or f32) maximum over the thread's 32 (16)
-//           logits of a tile is compared with theta's raw-logit bound; only
-//           hits get the reference's exact penalty / temperature arithmetic
-//           (sampling.cc:76-92) and enter a shared-memory buffer as 64-bit
-//           rank keys (value desc, token asc).  theta rises with the running
-//           maximum (min-p) and by exact compaction of the buffer;
+//   stream  read every tile once: per thread and tile the largest raw value
+//           of its 32 (16) logits, rounded up to bf16 (a bound kept in
+//           shared memory), and the thread's largest raw value with its
+//           column and penalty bit;
+//   theta   the exact values (sampling.cc:76-92) of the 256 threads' largest
+//           elements give theta: their k-th largest, a lower bound of the
+//           row's k-th largest value, and for min-p rows M + ln(min_p) -
+//           slack (M = their largest);
+//   gather  the blocks whose bound reaches theta's raw-logit bound are read
+//           again (from the ring when the unit is still whole there, else
+//           from L2) and their elements at or above theta enter a candidate
+//           buffer as 64-bit rank keys (value desc, token asc);
 //   finish  exact top-k and min-p cuts of the buffer, a sort, then the
 //           reference's softmax / top-p / draw (sampling.cc:105-145) in
 //           double precision with its sequential summation order.
@@ -1851,7 +1853,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             // lane j < m of warp 0 writes key j of the header (lane 0 also
             // its length, flags and k-th key), then arrives on the leader's
             // barrier itself: the leader waits for S * m arrivals
-            const uint32_t m = kHdrKeys / S;  // 8..32
+            const uint32_t m = kHdrKeys / S;  // 64 / kMaxSegs .. 32
             if (tid < m) {
                 if (tid == 0) {
                     const uint32_t kth = (r.k_eff && len >= r.k_eff)
@@ -1918,10 +1920,11 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             if (!(rflags & (kFTimeout | kFInf | kFOverflow))) {
                 uint32_t th = mkth;
                 if (r.minp) th = max(th, minp_key(mtop, r));
-                // warp w reads segment w's list down to the first entry below th
-                if (warp < S) {
-                    const uint32_t ls = c.xh_len[warp];
-                    const uint32_t src = cluster_addr(sorted, warp);
+                // warp w reads the lists of segments w, w + 8, ... down to
+                // the first entry below th
+                for (uint32_t s2 = warp; s2 < S; s2 += kCons / 32) {
+                    const uint32_t ls = c.xh_len[s2];
+                    const uint32_t src = cluster_addr(sorted, s2);
                     for (uint32_t i0 = 0; i0 < ls; i0 += 32) {
                         const uint32_t i = i0 + lane;
                         const uint64_t e = i < ls ? ld_cluster_u64(src + 8u * i) : 0ull;
@@ -2015,6 +2018,10 @@ static int launch_stream_t(const SampleArgs& a, void* stream) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem));
         if (e != cudaSuccess) return e;
+        if (kMaxSegs > 8) {  // clusters beyond the portable size
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return e;
+        }
         e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
         configured[slot][dev] = true;
