@@ -135,31 +135,44 @@ def bf16_tensor(arr, dev):
 
 
 def time_steps(step_fns, steps, stream, graph_len=32):
-    """Runs `steps` steps (step i calls step_fns[i % len]) inside CUDA graphs
-    of graph_len steps; returns elapsed ms measured with CUDA events on the
-    launch stream."""
+    """Runs `steps` steps (step i calls step_fns[i % len]) as CUDA graphs of
+    graph_len steps plus one graph of the remainder; returns elapsed ms
+    measured with CUDA events on the launch stream.  Each graph is replayed
+    once before the timed region (its first replay uploads it), so those
+    replays are untimed warm-up steps."""
     import torch
     n = len(step_fns)
     g_len = max(n, (graph_len // n) * n)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        with torch.cuda.graph(g, stream=stream):
-            for i in range(g_len):
-                step_fns[i % n](stream)
-    torch.cuda.synchronize()
     full, rest = divmod(steps, g_len)
+
+    def capture(count):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(count):
+                    step_fns[i % n](stream)
+        return g
+
+    g = capture(g_len) if full else None
+    g_rest = capture(rest) if rest else None
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for x in (g, g_rest):
+            if x is not None:
+                x.replay()
+    torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         t0.record(stream)
         for _ in range(full):
             g.replay()
-        for i in range(rest):
-            step_fns[i % n](stream)
+        if g_rest is not None:
+            g_rest.replay()
         t1.record(stream)
     t1.synchronize()
     ms = t0.elapsed_time(t1)
-    del g
+    del g, g_rest
     return ms
 
 
