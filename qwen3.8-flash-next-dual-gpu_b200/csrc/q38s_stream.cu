@@ -1013,7 +1013,9 @@ __device__ void mtp_finish(const SampleArgs& a, unsigned char* area, Ctl& c) {
 __device__ void row_done(const SampleArgs& a, unsigned char* area, Ctl& c) {
     if (!a.mtp) return;
     cbar();
-    // one GPU-scope acquire-release ticket (see the segment merge)
+    // one GPU-scope acquire-release ticket: it publishes this row's outputs
+    // (ordered before it by the barrier) and, for the last row, makes every
+    // other row's visible
     if (threadIdx.x == 0) {
         c.bc_u32[2] = atom_add_acq_rel_gpu(a.ticket, 1u) == a.vrows - 1;
     }
