@@ -332,10 +332,14 @@ def test_batch_commit_checks_state(cuda):
 
 
 # ------------------------------------------------------------- extensions
-def test_mtp_q_equals_p_accepts_every_draft(cuda):
+@pytest.mark.parametrize("n", [16, 20, 36])
+def test_mtp_q_equals_p_accepts_every_draft(n, cuda):
+    """q = p accepts every draft.  16, 20 and 36 drafts give 33, 41 and 73
+    virtual rows, split into 8, 7 and 4 segments per row (a cluster each),
+    more clusters than fit on the GPU at once."""
     import torch
     rng = np.random.default_rng(31)
-    vocab, n = synth.VOCAB, 16
+    vocab = synth.VOCAB
     cfg = q38s.config_v2(top_k=20, top_p=0.95, temperature=0.7, seed=12345)
     target = rng.normal(0, 3, (n + 1, vocab)).astype(np.float32)
     p = oracle_params(cfg, cfg.seed)

@@ -134,3 +134,29 @@ def test_wide_unit_takes_general_path(cuda):
                q38s.config_v2(top_k=0, top_p=0.95, min_p=0.05, temperature=1.0, seed=12)]
     hists = [rng.integers(0, vocab, 2000).astype(np.int32) for _ in range(2)]
     assert check_batch(configs, logits, hists, cuda) == 0
+
+
+@pytest.mark.parametrize("rows", [42, 49, 59, 74, 98])
+def test_cluster_sizes_three_to_seven(rows, cuda):
+    """Batches of 42, 49, 59, 74 and 98 rows split every row into 7, 6, 5, 4
+    and 3 column segments (one cluster per row): headers of 64 // S keys,
+    the rank-based merge bound, the leader's reads of every segment's list.
+    Mixed top-k (with and without min-p), penalties and temperatures."""
+    rng = np.random.default_rng(3000 + rows)
+    vocab = 20000
+    x = spiked_rows(rng, rows, vocab, spikes=24)
+    logits = synth.f32_to_bf16_rne(x)
+    ks = [1, 3, 20, 40, 64, 100, 200, 256, 0]
+    configs = []
+    for r in range(rows):
+        k = ks[r % len(ks)]
+        configs.append(q38s.config_v2(
+            top_k=k, top_p=float(rng.uniform(0.5, 1.0)),
+            min_p=0.05 if k == 0 else float(rng.choice([0.0, 0.02])),
+            temperature=float(rng.uniform(0.3, 1.2)),
+            repetition_penalty=float(rng.uniform(1.0, 1.2)),
+            presence_penalty=float(rng.choice([0.0, 0.4])),
+            seed=int(rng.integers(1, 2**63))))
+    hists = [rng.integers(0, vocab, int(rng.integers(1, 2000))).astype(np.int32)
+             for _ in range(rows)]
+    assert check_batch(configs, logits, hists, cuda) == 0
