@@ -436,24 +436,6 @@ __device__ __forceinline__ void hist_inc(uint32_t* hist, uint32_t bin, bool acti
             atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
     }
 }
-// Same with a fixed-point mass per lane (below 2^44): the lanes of a bin
-// add their masses exactly as two 22-bit limbs with warp reductions, and one
-// lane per bin updates the shared counters.  The whole warp calls it.
-__device__ __forceinline__ void hist_inc_mass(uint32_t* hist, uint64_t* hmass, uint32_t bin,
-                                              uint64_t mass, bool active) {
-    const uint32_t act = __ballot_sync(0xffffffffu, active);
-    if (active) {
-        const uint32_t peers = __match_any_sync(act, bin);
-        const uint32_t lo = __reduce_add_sync(peers, static_cast<uint32_t>(mass & 0x3fffffu));
-        const uint32_t hi = __reduce_add_sync(peers, static_cast<uint32_t>(mass >> 22));
-        if ((threadIdx.x & 31) == static_cast<uint32_t>(__ffs(peers) - 1)) {
-            atomicAdd(&hist[bin], static_cast<uint32_t>(__popc(peers)));
-            atomicAdd(reinterpret_cast<unsigned long long*>(&hmass[bin]),
-                      static_cast<unsigned long long>(lo) +
-                          (static_cast<unsigned long long>(hi) << 22));
-        }
-    }
-}
 // Appends `key` for every lane with `push` set; one atomic per warp.  The
 // whole warp calls it.  Returns true when the buffer overflowed.
 __device__ __forceinline__ bool warp_push(bool push, uint64_t key, uint64_t* buf, uint32_t cap,
@@ -1092,9 +1074,37 @@ struct Sel {
 // first element in canonical order (value desc, token asc) at which the
 // running count (wts == null) or fixed-point mass (wts: the stored weights)
 // reaches tau (>= tau, or > tau when strict).
+// The histograms of a pass are per-warp rows in the work area (free while
+// the general path selects): every active lane adds its count and mass to
+// its warp's row with shared-memory atomics (exact integer sums), and the
+// rows are summed per bin after the pass.
 __device__ Sel row_select(const uint32_t* keys, const float* wts, uint32_t V, uint32_t tok0,
-                          const Cut& g0, bool restrict_k0, uint64_t tau, bool strict, Ctl& c) {
+                          const Cut& g0, bool restrict_k0, uint64_t tau, bool strict,
+                          unsigned char* area, Ctl& c) {
     const bool weighted = wts != nullptr;
+    constexpr uint32_t kW = kCons / 32;
+    uint32_t* whist = reinterpret_cast<uint32_t*>(area);                    // [kW][256]
+    unsigned long long* wmass =
+        reinterpret_cast<unsigned long long*>(area + kW * 256 * 4);         // [kW][256]
+    uint32_t* myhist = whist + (threadIdx.x >> 5) * 256;
+    unsigned long long* mymass = wmass + (threadIdx.x >> 5) * 256;
+    auto clear_rows = [&]() {
+        for (uint32_t i = threadIdx.x; i < kW * 256; i += kCons) {
+            whist[i] = 0;
+            wmass[i] = 0;
+        }
+    };
+    auto sum_rows = [&]() {  // bin threadIdx.x over the warps' rows
+        uint32_t h = 0;
+        uint64_t m = 0;
+#pragma unroll
+        for (uint32_t w = 0; w < kW; ++w) {
+            h += whist[w * 256 + threadIdx.x];
+            m += wmass[w * 256 + threadIdx.x];
+        }
+        c.hist[threadIdx.x] = h;
+        c.hmass[threadIdx.x] = m;
+    };
     Cut g = g0;
     if (!restrict_k0) g.has_cut = false;
     uint32_t prefix = 0, mask = 0;
@@ -1104,15 +1114,17 @@ __device__ Sel row_select(const uint32_t* keys, const float* wts, uint32_t V, ui
     for (int level = 0; level < 4; ++level) {
         const int shift = 24 - 8 * level;
         cbar();
-        c.hist[threadIdx.x] = 0;
-        c.hmass[threadIdx.x] = 0;
+        clear_rows();
         cbar();
         for_keys(keys, wts, V, [&](uint32_t j, uint32_t key, float w, bool valid) {
-            const bool act = valid && (key & mask) == prefix && in_k0(g, key, tok0 + j);
-            const uint32_t d = (key >> shift) & 255u;
-            if (weighted) hist_inc_mass(c.hist, c.hmass, d, act ? wfix(w) : 0ull, act);
-            else hist_inc(c.hist, d, act);
+            if (valid && (key & mask) == prefix && in_k0(g, key, tok0 + j)) {
+                const uint32_t d = (key >> shift) & 255u;
+                atomicAdd(&myhist[d], 1u);
+                if (weighted) atomicAdd(&mymass[d], static_cast<unsigned long long>(wfix(w)));
+            }
         });
+        cbar();
+        sum_rows();
         cbar();
         if (threadIdx.x == 0) {
             uint64_t acc = above;
@@ -1170,14 +1182,15 @@ __device__ Sel row_select(const uint32_t* keys, const float* wts, uint32_t V, ui
         for (int level = 0; level < 4; ++level) {
             const int shift = 24 - 8 * level;
             cbar();
-            c.hist[threadIdx.x] = 0;
+            clear_rows();
             cbar();
             for_keys(keys, nullptr, V, [&](uint32_t x, uint32_t k2, float, bool valid) {
                 const uint32_t tok = tok0 + x;
-                const bool act =
-                    valid && k2 == key && (tok & tmask) == tprefix && in_k0(g, key, tok);
-                hist_inc(c.hist, (tok >> shift) & 255u, act);
+                if (valid && k2 == key && (tok & tmask) == tprefix && in_k0(g, key, tok))
+                    atomicAdd(&myhist[(tok >> shift) & 255u], 1u);
             });
+            cbar();
+            sum_rows();
             cbar();
             if (threadIdx.x == 0) {
                 uint32_t left = need, d = 0;
@@ -1291,7 +1304,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
     const uint32_t c_minp = csum_u32(cnt, c);
     const uint32_t n0 = r.k_eff ? min(r.k_eff, c_minp) : c_minp;
     if (n0 < c_minp) {
-        const Sel cut = row_select(keys, nullptr, V, tok0, g, false, n0, false, c);
+        const Sel cut = row_select(keys, nullptr, V, tok0, g, false, n0, false, area, c);
         g.has_cut = true;
         g.cut_key = cut.key;
         g.cut_tok = cut.token;
@@ -1337,7 +1350,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
     if (status == Q38S_ROW_OK && r.p.top_p < 1.0f) {
         const uint64_t tau = static_cast<uint64_t>(static_cast<double>(r.p.top_p) *
                                                    static_cast<double>(Z));
-        cutp = row_select(keys, wts, V, tok0, g, true, tau, false, c);
+        cutp = row_select(keys, wts, V, tok0, g, true, tau, false, area, c);
         if (cutp.found) Zr = cutp.through;
     }
     Q38S_TT(r.v, 14);
@@ -1346,7 +1359,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         const double u = uniform01(r.rng_before + kGamma);
         const uint64_t draw = static_cast<uint64_t>(u * static_cast<double>(Zr));
         draw_d = static_cast<double>(draw) / kFix;
-        const Sel sel = row_select(keys, wts, V, tok0, g, true, draw, true, c);
+        const Sel sel = row_select(keys, wts, V, tok0, g, true, draw, true, area, c);
         if (sel.found) token = static_cast<int32_t>(sel.token);
         else if (cutp.found) token = static_cast<int32_t>(cutp.token);
         else status = Q38S_ROW_NORMALIZATION;
