@@ -1074,37 +1074,52 @@ struct Sel {
 // first element in canonical order (value desc, token asc) at which the
 // running count (wts == null) or fixed-point mass (wts: the stored weights)
 // reaches tau (>= tau, or > tau when strict).
-// The histograms of a pass are per-warp rows in the work area (free while
-// the general path selects): every active lane adds its count and mass to
-// its warp's row with shared-memory atomics (exact integer sums), and the
-// rows are summed per bin after the pass.
-__device__ Sel row_select(const uint32_t* keys, const float* wts, uint32_t V, uint32_t tok0,
-                          const Cut& g0, bool restrict_k0, uint64_t tau, bool strict,
-                          unsigned char* area, Ctl& c) {
-    const bool weighted = wts != nullptr;
-    constexpr uint32_t kW = kCons / 32;
-    uint32_t* whist = reinterpret_cast<uint32_t*>(area);                    // [kW][256]
-    unsigned long long* wmass =
-        reinterpret_cast<unsigned long long*>(area + kW * 256 * 4);         // [kW][256]
-    uint32_t* myhist = whist + (threadIdx.x >> 5) * 256;
-    unsigned long long* mymass = wmass + (threadIdx.x >> 5) * 256;
-    auto clear_rows = [&]() {
-        for (uint32_t i = threadIdx.x; i < kW * 256; i += kCons) {
-            whist[i] = 0;
-            wmass[i] = 0;
+// The general path's histograms: per-warp rows of 256 bins (counts, then
+// fixed-point masses) in the work area, which is free while the general
+// path selects.  Every active lane adds its count and mass to its warp's
+// row with shared-memory atomics (exact integer sums); the rows are summed
+// per bin after a pass.  A saved histogram (counts, masses) follows them.
+constexpr uint32_t kRowsW = kCons / 32;
+constexpr uint32_t kSaved = kRowsW * 256 * 12;  // byte offset of the saved histogram
+static_assert(kSaved + 256 * 12 <= kArea, "general-path histograms");
+struct HistRows {
+    uint32_t* hist;            // [kRowsW][256]
+    unsigned long long* mass;  // [kRowsW][256]
+    __device__ explicit HistRows(unsigned char* area)
+        : hist(reinterpret_cast<uint32_t*>(area)),
+          mass(reinterpret_cast<unsigned long long*>(area + kRowsW * 256 * 4)) {}
+    __device__ void clear() {
+        for (uint32_t i = threadIdx.x; i < kRowsW * 256; i += kCons) {
+            hist[i] = 0;
+            mass[i] = 0;
         }
-    };
-    auto sum_rows = [&]() {  // bin threadIdx.x over the warps' rows
+    }
+    __device__ void add(uint32_t bin, uint64_t m, bool weighted) {
+        const uint32_t row = (threadIdx.x >> 5) * 256;
+        atomicAdd(&hist[row + bin], 1u);
+        if (weighted) atomicAdd(&mass[row + bin], static_cast<unsigned long long>(m));
+    }
+    __device__ void sum(Ctl& c) {  // bin threadIdx.x over the warps' rows
         uint32_t h = 0;
         uint64_t m = 0;
 #pragma unroll
-        for (uint32_t w = 0; w < kW; ++w) {
-            h += whist[w * 256 + threadIdx.x];
-            m += wmass[w * 256 + threadIdx.x];
+        for (uint32_t w = 0; w < kRowsW; ++w) {
+            h += hist[w * 256 + threadIdx.x];
+            m += mass[w * 256 + threadIdx.x];
         }
         c.hist[threadIdx.x] = h;
         c.hmass[threadIdx.x] = m;
-    };
+    }
+};
+
+// l0: a saved first-level histogram (counts, then masses, 256 each) of the
+// same keys, restriction and weights, used instead of the first pass (or
+// null).
+__device__ Sel row_select(const uint32_t* keys, const float* wts, uint32_t V, uint32_t tok0,
+                          const Cut& g0, bool restrict_k0, uint64_t tau, bool strict,
+                          unsigned char* area, const unsigned char* l0, Ctl& c) {
+    const bool weighted = wts != nullptr;
+    HistRows rows(area);
     Cut g = g0;
     if (!restrict_k0) g.has_cut = false;
     uint32_t prefix = 0, mask = 0;
@@ -1114,17 +1129,19 @@ __device__ Sel row_select(const uint32_t* keys, const float* wts, uint32_t V, ui
     for (int level = 0; level < 4; ++level) {
         const int shift = 24 - 8 * level;
         cbar();
-        clear_rows();
-        cbar();
-        for_keys(keys, wts, V, [&](uint32_t j, uint32_t key, float w, bool valid) {
-            if (valid && (key & mask) == prefix && in_k0(g, key, tok0 + j)) {
-                const uint32_t d = (key >> shift) & 255u;
-                atomicAdd(&myhist[d], 1u);
-                if (weighted) atomicAdd(&mymass[d], static_cast<unsigned long long>(wfix(w)));
-            }
-        });
-        cbar();
-        sum_rows();
+        if (level == 0 && l0) {
+            c.hist[threadIdx.x] = reinterpret_cast<const uint32_t*>(l0)[threadIdx.x];
+            c.hmass[threadIdx.x] = reinterpret_cast<const uint64_t*>(l0 + 1024)[threadIdx.x];
+        } else {
+            rows.clear();
+            cbar();
+            for_keys(keys, wts, V, [&](uint32_t j, uint32_t key, float w, bool valid) {
+                if (valid && (key & mask) == prefix && in_k0(g, key, tok0 + j))
+                    rows.add((key >> shift) & 255u, weighted ? wfix(w) : 0ull, weighted);
+            });
+            cbar();
+            rows.sum(c);
+        }
         cbar();
         if (threadIdx.x == 0) {
             uint64_t acc = above;
@@ -1182,15 +1199,15 @@ __device__ Sel row_select(const uint32_t* keys, const float* wts, uint32_t V, ui
         for (int level = 0; level < 4; ++level) {
             const int shift = 24 - 8 * level;
             cbar();
-            clear_rows();
+            rows.clear();
             cbar();
             for_keys(keys, nullptr, V, [&](uint32_t x, uint32_t k2, float, bool valid) {
                 const uint32_t tok = tok0 + x;
                 if (valid && k2 == key && (tok & tmask) == tprefix && in_k0(g, key, tok))
-                    atomicAdd(&myhist[(tok >> shift) & 255u], 1u);
+                    rows.add((tok >> shift) & 255u, 0ull, false);
             });
             cbar();
-            sum_rows();
+            rows.sum(c);
             cbar();
             if (threadIdx.x == 0) {
                 uint32_t left = need, d = 0;
@@ -1304,7 +1321,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
     const uint32_t c_minp = csum_u32(cnt, c);
     const uint32_t n0 = r.k_eff ? min(r.k_eff, c_minp) : c_minp;
     if (n0 < c_minp) {
-        const Sel cut = row_select(keys, nullptr, V, tok0, g, false, n0, false, area, c);
+        const Sel cut = row_select(keys, nullptr, V, tok0, g, false, n0, false, area, nullptr, c);
         g.has_cut = true;
         g.cut_key = cut.key;
         g.cut_tok = cut.token;
@@ -1332,15 +1349,26 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
     }
     // G4: large kept set: weights once (float), then fixed-point masses
     // (2^-43 units) locate the top-p cut and the draw
+    // (and the first-level histogram of both weighted selections below: the
+    // same keys, restriction and weights)
     uint64_t part = 0;
+    HistRows rows(area);
+    cbar();
+    rows.clear();
+    cbar();
     for_keys(keys, nullptr, V, [&](uint32_t j, uint32_t k, float, bool valid) {
         if (!valid) return;
         const bool in = in_k0(g, k, tok0 + j);
         const float w = in ? weight_of(k, g.M) : 0.0f;
         wts[j] = w;
         part += wfix(w);
+        if (in) rows.add(k >> 24, wfix(w), true);
     });
-    const uint64_t Z = csum_u64(part, c);  // its barriers also publish wts[]
+    const uint64_t Z = csum_u64(part, c);  // its barriers also publish wts[] and the rows
+    rows.sum(c);
+    reinterpret_cast<uint32_t*>(area + kSaved)[threadIdx.x] = c.hist[threadIdx.x];
+    reinterpret_cast<uint64_t*>(area + kSaved + 1024)[threadIdx.x] = c.hmass[threadIdx.x];
+    cbar();
     Q38S_TT(r.v, 13);
     int32_t status = Q38S_ROW_OK;
     int32_t token = -1;
@@ -1350,7 +1378,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
     if (status == Q38S_ROW_OK && r.p.top_p < 1.0f) {
         const uint64_t tau = static_cast<uint64_t>(static_cast<double>(r.p.top_p) *
                                                    static_cast<double>(Z));
-        cutp = row_select(keys, wts, V, tok0, g, true, tau, false, area, c);
+        cutp = row_select(keys, wts, V, tok0, g, true, tau, false, area, area + kSaved, c);
         if (cutp.found) Zr = cutp.through;
     }
     Q38S_TT(r.v, 14);
@@ -1359,7 +1387,7 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         const double u = uniform01(r.rng_before + kGamma);
         const uint64_t draw = static_cast<uint64_t>(u * static_cast<double>(Zr));
         draw_d = static_cast<double>(draw) / kFix;
-        const Sel sel = row_select(keys, wts, V, tok0, g, true, draw, true, area, c);
+        const Sel sel = row_select(keys, wts, V, tok0, g, true, draw, true, area, area + kSaved, c);
         if (sel.found) token = static_cast<int32_t>(sel.token);
         else if (cutp.found) token = static_cast<int32_t>(cutp.token);
         else status = Q38S_ROW_NORMALIZATION;
