@@ -58,7 +58,7 @@ constexpr uint32_t kRing = 4;                    // ring slots per CTA
 constexpr int kCons = 256;                       // consumer threads (warps 0-7)
 constexpr int kBlock = kCons + 32;               // + the producer warp
 constexpr uint32_t kBuf = 2048;                  // candidate buffer (rank keys)
-constexpr uint32_t kFinal = 512;                 // candidates entering the epilogue
+constexpr uint32_t kFinal = 1024;                // candidates entering the epilogue
 constexpr uint32_t kGather = 1024;               // exact gather of the general path
 constexpr uint32_t kArea = 32768;                // candidate / epilogue work area
 constexpr double kFix = 8796093022208.0;         // 2^43: fixed-point weight unit
@@ -69,7 +69,12 @@ constexpr uint32_t kFOverflow = 1u;
 constexpr uint32_t kFInf = 2u;
 constexpr uint32_t kFTimeout = 4u;
 
-static_assert(kBuf * 8 + kFinal * 8 + 3 * kFinal * 8 <= kArea, "fast-path area");
+// Fast-path layout of the area: the candidate buffer (kBuf keys) and, once
+// it is sorted, the epilogue's three double arrays (w, S, q) from offset 0;
+// the sorted list (kFinal keys) at kSorted; the per-thread tile bounds at
+// the tail while a unit streams (dead before the list is sorted).
+constexpr uint32_t kSorted = 3 * kFinal * 8;
+static_assert(kBuf * 8 <= kSorted && kSorted + kFinal * 8 <= kArea, "fast-path area");
 
 // Optional per-unit trace (build with -DQ38S_TRACE; off in the product
 // build): 16 words per unit -- global-timer stamps of the unit's phases, its
@@ -1413,7 +1418,7 @@ __device__ void finish_row(const SampleArgs& a, const Row& r, uint32_t flags,
     } else if (flags & kFOverflow) {
         general_row<DT>(a, r, area, c);
     } else {
-        double* w = reinterpret_cast<double*>(area + (kBuf + kFinal) * 8);
+        double* w = reinterpret_cast<double*>(area);  // over the dead candidate buffer
         row_output(a, r, sorted, keep, w, w + kFinal, w + 2 * kFinal, c);
     }
     row_done(a, area, c);
@@ -1502,7 +1507,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
     unsigned char* ring = dsm;
     unsigned char* area = dsm + kRing * kSlot;
     uint64_t* cand = reinterpret_cast<uint64_t*>(area);
-    uint64_t* sorted = cand + kBuf;
+    uint64_t* sorted = reinterpret_cast<uint64_t*>(area + kSorted);
     const uint32_t tid = threadIdx.x;
 
     if (tid == 0) {
