@@ -185,8 +185,10 @@ def run_ours(args, rank, world, dist):
     stream = torch.cuda.Stream(dev)
     peak, peak_kind = load_peaks()
 
-    # ---- configuration 4 on this rank (weak scaling: own 256 rows)
-    spec = synth.cfg4_spec(seed=4 + 1000 * rank)
+    # ---- configuration 4 on this rank (weak scaling: own 256 rows).  Every
+    # rank samples the same row specification (parameters, histories: the
+    # single-GPU draw) on its own logits, so each GPU does the same work.
+    spec = synth.cfg4_spec(seed=4)
     configs = cfg4_configs(q38s, spec)
     batch = q38s.Batch(VOCAB, configs, device=dev.index)
     batch.commit_tokens(spec.histories)
@@ -276,6 +278,8 @@ def run_ours(args, rank, world, dist):
                                "U{1..32768}; step = prepare + commit + commit_token",
                    "rows_per_gpu": ROWS, "vocab": VOCAB, "global_batch": rows_total,
                    "parallelism": f"row-sharded x{world} (no collective)",
+                   "rows": "every rank: the same row parameters and histories (seed 4), "
+                           "its own logits (seed 4 + 1000 * rank)",
                    "l2": f"inputs rotate over {N_INPUT_BATCHES} batches "
                          f"({N_INPUT_BATCHES * ROWS * ROW_BYTES_BF16 / 1e6:.0f} MB > 126 MB L2)",
                    "timing": "CUDA graphs of 32 steps, CUDA events on the launch stream, "
