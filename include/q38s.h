@@ -300,6 +300,20 @@ int q38s_argmax_bf16(const uint16_t* logits, uint32_t count, int32_t* output,
                      void* stream, int device);
 
 /* ------------------------------------------------------------------------
+ * Failure injection, for tests of the bounded device waits only.  No
+ * counterpart in the reference (its sampler runs on the host and has no
+ * device waits).
+ *
+ * With withhold_copies != 0, every later sampling launch of this process
+ * has its first CTA issue no logit copy, and that CTA's consumers give up
+ * waiting for a tile after wait_cycles SM clock cycles: the wait runs out on
+ * a barrier nothing completes, with no copy in flight.  The rows of that CTA
+ * report Q38S_ROW_TIMEOUT (a one-session prepare returns Q38S_TIMEOUT); the
+ * others are sampled normally.  withhold_copies = 0 restores normal
+ * operation.  Not thread-safe; never set in production. */
+int q38s_testing_set_fault(uint32_t withhold_copies, uint64_t wait_cycles);
+
+/* ------------------------------------------------------------------------
  * Sampling without device allocation.  No counterpart in the reference.
  *
  * For callers that must not allocate GPU memory themselves or through this
@@ -307,9 +321,9 @@ int q38s_argmax_bf16(const uint16_t* logits, uint32_t count, int32_t* output,
  * plug-in loaded into a host process that forbids cudaMalloc after start-up,
  * or a real-time loop in which an allocation (and the device-wide
  * synchronisation it can cause) is not allowed.  Every working buffer lives
- * in one fixed, statically sized device array inside this library (about
- * 10.6 MB on every GPU that loads it, held until the process exits); the
- * caller passes only inputs and outputs.
+ * in one fixed, statically sized device array inside this library
+ * (8,520,192 bytes on every GPU that loads it, held until the process
+ * exits); the caller passes only inputs and outputs.
  *
  * prepare() (sampling.cc:59-146 plus min_p) for `rows` rows of device logits
  * (row r at logits + r * row_stride elements, bf16 or f32) as freshly
@@ -321,11 +335,15 @@ int q38s_argmax_bf16(const uint16_t* logits, uint32_t count, int32_t* output,
  * seed.  decisions: device array of `rows` entries.  The result equals
  * q38s_batch_prepare on a new batch with the same configs and states.
  * Limits: 1 <= rows <= 4, vocabulary <= 262,144; larger sizes are rejected
- * with Q38S_INVALID_ARGUMENT.  The first call on a device resolves and
- * clears the static array (a synchronous step: make that first call before
- * any stream capture).  Every call shares the array, so calls whose work
- * overlaps on the GPU (other streams, other host threads) race; order them
- * on one stream. */
+ * with Q38S_INVALID_ARGUMENT.  Host arrays are read before the call
+ * returns (the rows reach the device as kernel arguments).  The first call
+ * on a device looks up the static array's device address
+ * (cudaGetSymbolAddress, which may load this library's device code and
+ * synchronise): make that first call before any stream capture.  Every
+ * call shares the array and leaves its contents behind (each call rewrites
+ * the rows' parameters and clears their penalty bitmaps first), so calls
+ * whose work overlaps on the GPU (other streams, other host threads) race;
+ * order them on one stream. */
 int q38s_prepare_noalloc(const void* logits, uint16_t dtype, uint32_t vocabulary,
                          uint32_t rows, uint64_t row_stride,
                          const q38s_sampling_config_v2* configs,

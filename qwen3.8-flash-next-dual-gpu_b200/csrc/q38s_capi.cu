@@ -817,6 +817,13 @@ int q38s_sampler_config(const q38s_sampler* s, q38s_sampling_config_v1* out) {
     return ok();
 }
 
+int q38s_testing_set_fault(uint32_t withhold_copies, uint64_t wait_cycles) {
+    if (withhold_copies && (wait_cycles == 0 || wait_cycles > 4000000000ull))
+        return fail(Q38S_INVALID_ARGUMENT, "fault wait must be 1 to 4e9 cycles");
+    set_stream_fault(withhold_copies ? 1u : 0u, static_cast<long long>(wait_cycles));
+    return ok();
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------ no-allocation entry
@@ -834,7 +841,7 @@ constexpr uint32_t kNoAllocBitmapWords = ((kNoAllocVocab + 127) / 128) * 4;
 struct NoAllocLayout {  // byte offsets into the static array
     static constexpr size_t params = 0;
     static constexpr size_t state = params + 256;
-    static constexpr size_t bitmap = state + 256;  // zeros
+    static constexpr size_t bitmap = state + 256;  // cleared per call
     static constexpr size_t keys =
         bitmap + sizeof(uint32_t) * static_cast<size_t>(kNoAllocBitmapWords) * kNoAllocRows;
     static constexpr size_t weights =
@@ -851,15 +858,36 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[NoAllocLayout::
 std::mutex g_noalloc_mu;
 unsigned char* g_noalloc_ptr[64] = {};  // device address per device ordinal
 
-// Once per device, with that device current: the array's device address,
-// and the zero penalty bitmap the kernel expects.
+// The rows of one call, handed to the device as kernel arguments: nothing is
+// read from host memory after the launch returns.
+struct NoAllocRows {
+    RowParams params[kNoAllocRows];
+    RowState states[kNoAllocRows];
+};
+
+// Writes the call's parameters and states into the array and clears the
+// rows' penalty bitmaps (calls share the array; a fresh sampler has no
+// history).  Ordered before the sampling kernel on the caller's stream.
+__global__ void noalloc_stage_kernel(NoAllocRows in, uint32_t rows, uint32_t bitmap_words,
+                                     unsigned char* base) {
+    const uint32_t tid = blockIdx.x * blockDim.x + threadIdx.x;
+    if (tid < rows) {
+        reinterpret_cast<RowParams*>(base + NoAllocLayout::params)[tid] = in.params[tid];
+        reinterpret_cast<RowState*>(base + NoAllocLayout::state)[tid] = in.states[tid];
+    }
+    uint32_t* bm = reinterpret_cast<uint32_t*>(base + NoAllocLayout::bitmap);
+    const uint32_t n = rows * bitmap_words;
+    for (uint32_t i = tid; i < n; i += gridDim.x * blockDim.x) bm[i] = 0u;
+}
+
+// Once per device, with that device current: the array's device address.
+// (cudaGetSymbolAddress may load this library's device code on first use.)
 int noalloc_setup(int device, unsigned char** out) {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     if (device < 0 || device >= 64) return fail(Q38S_CUDA_ERROR, "device ordinal out of range");
     if (!g_noalloc_ptr[device]) {
         void* p = nullptr;
         Q38S_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch), "no-alloc scratch address");
-        Q38S_CUDA(cudaMemset(p, 0, NoAllocLayout::end), "no-alloc scratch clear");
         g_noalloc_ptr[device] = static_cast<unsigned char*>(p);
     }
     *out = g_noalloc_ptr[device];
@@ -883,14 +911,14 @@ extern "C" int q38s_prepare_noalloc(const void* logits, uint16_t dtype, uint32_t
     if (dtype != Q38S_DTYPE_BF16 && dtype != Q38S_DTYPE_F32)
         return fail(Q38S_INVALID_ARGUMENT, "logits dtype must be bf16 or f32");
     if (row_stride < vocabulary) return fail(Q38S_INVALID_ARGUMENT, kMsgSize);
-    RowParams params[kNoAllocRows];
-    RowState states[kNoAllocRows];
+    NoAllocRows in;
+    std::memset(&in, 0, sizeof(in));
     for (uint32_t r = 0; r < rows; ++r) {
         const int rc = validate_config(vocabulary, 2, configs[r]);
         if (rc) return rc;
         if (configs[r].mode == Q38S_MODE_GREEDY) return fail(Q38S_LOGIC_ERROR, kMsgGreedy);
-        params[r] = to_params(configs[r]);
-        states[r] = RowState{rng_states ? rng_states[r] : configs[r].seed, 0, 0, 0};
+        in.params[r] = to_params(configs[r]);
+        in.states[r] = RowState{rng_states ? rng_states[r] : configs[r].seed, 0, 0, 0};
     }
     int device = 0;
     Q38S_CUDA(cudaGetDevice(&device), "current device");
@@ -898,13 +926,9 @@ extern "C" int q38s_prepare_noalloc(const void* logits, uint16_t dtype, uint32_t
     int rc = noalloc_setup(device, &base);
     if (rc) return rc;
     auto s = static_cast<cudaStream_t>(stream);
-    // per-call inputs into the array
-    Q38S_CUDA(cudaMemcpyAsync(base + NoAllocLayout::params, params, sizeof(RowParams) * rows,
-                              cudaMemcpyHostToDevice, s),
-              "no-alloc parameters");
-    Q38S_CUDA(cudaMemcpyAsync(base + NoAllocLayout::state, states, sizeof(RowState) * rows,
-                              cudaMemcpyHostToDevice, s),
-              "no-alloc states");
+    const uint32_t bitmap_words = ((vocabulary + 127) / 128) * 4;
+    noalloc_stage_kernel<<<8, 256, 0, s>>>(in, rows, bitmap_words, base);
+    Q38S_CUDA(cudaGetLastError(), "no-alloc staging");
     const uint32_t es = dtype == Q38S_DTYPE_BF16 ? 2u : 4u;
     SampleArgs a;
     std::memset(&a, 0, sizeof(a));
@@ -922,7 +946,7 @@ extern "C" int q38s_prepare_noalloc(const void* logits, uint16_t dtype, uint32_t
     a.params = reinterpret_cast<const RowParams*>(base + NoAllocLayout::params);
     a.state = reinterpret_cast<RowState*>(base + NoAllocLayout::state);
     a.bitmap = reinterpret_cast<uint32_t*>(base + NoAllocLayout::bitmap);
-    a.bitmap_words = ((vocabulary + 127) / 128) * 4;
+    a.bitmap_words = bitmap_words;
     a.counts = nullptr;  // no history: every count is zero
     a.vrow_state_const = ~0u;
     a.decisions = decisions;

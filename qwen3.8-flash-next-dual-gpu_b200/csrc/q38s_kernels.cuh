@@ -87,6 +87,12 @@ struct SampleArgs {
     // segs CTAs, one cluster per row, and the segments' lists are merged
     // in the cluster's shared memory
     uint32_t segs;
+    // failure injection for the tests of the bounded waits (0 in normal
+    // use): with test_withhold set, the producer of CTA 0 issues no copy and
+    // that CTA's consumers give up on a tile after test_wait_cycles, so the
+    // wait runs out on a barrier nothing completes, with no copy in flight
+    uint32_t test_withhold;
+    long long test_wait_cycles;
 };
 
 // Most segments per row: one cluster per split row (8 is the portable
@@ -95,6 +101,9 @@ constexpr uint32_t kMaxSegs = 8;
 
 // Launchers (q38s_stream.cu, q38s_sample.cu).  All return a cudaError_t as int.
 int launch_stream(const SampleArgs& a, void* stream);   // streaming sampler
+// Failure injection applied to every later stream-kernel launch of the
+// process (tests only; withhold 0 turns it off).
+void set_stream_fault(uint32_t withhold, long long wait_cycles);
 uint32_t stream_segments(uint32_t vrows, uint32_t vocab, int device);
 int launch_commit_tokens(RowState* state, uint32_t* bitmap, uint32_t bitmap_words,
                          uint32_t* counts, uint32_t vocab, uint32_t col_begin,

@@ -1434,12 +1434,12 @@ __device__ __forceinline__ void chunk_range(uint32_t vocab, uint32_t S, uint32_t
     hi = min(b1 * 128u, vocab);
 }
 
-__device__ bool wait_full(Ctl& c, uint32_t slot, uint32_t phase) {
+__device__ bool wait_full(Ctl& c, uint32_t slot, uint32_t phase, long long limit) {
     if (mbar_try_wait(&c.full[slot], phase)) return true;
     const long long start = clock64();
     while (!mbar_try_wait(&c.full[slot], phase)) {
         if (*reinterpret_cast<volatile uint32_t*>(&c.abort_flag)) return false;
-        if (clock64() - start > kWaitLimitCycles) return false;
+        if (clock64() - start > limit) return false;
     }
     return true;
 }
@@ -1452,6 +1452,10 @@ __device__ void produce(const SampleArgs& a, unsigned char* ring, Ctl& c) {
     constexpr uint32_t TC = kTileBytes / es;
     const uint32_t S = a.segs;
     const uint32_t n_units = a.vrows * S;
+    if (a.test_withhold && blockIdx.x == 0) {  // failure injection: no copy at all
+        atomicExch(&c.prod_done, 1u);
+        return;
+    }
     uint32_t g = 0;
     for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
         const uint32_t v = u / S;
@@ -1550,6 +1554,8 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
     const uint32_t n_units = a.vrows * S;
     uint32_t g = 0;     // tiles passed (the producer's order)
     uint32_t xrow = 0;  // multi-segment rows passed (the cluster barriers' parity)
+    const long long tile_wait =
+        (a.test_withhold && blockIdx.x == 0) ? a.test_wait_cycles : kWaitLimitCycles;
     bool stop = false;  // this warp gave up on a copy (warp-uniform)
     (void)warp;
     for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
@@ -1585,7 +1591,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
 #ifdef Q38S_TRACE
             const long long tw0 = clock64();
 #endif
-            bool ok = !stop && wait_full(c, slot, (g / kRing) & 1u);
+            bool ok = !stop && wait_full(c, slot, (g / kRing) & 1u, tile_wait);
 #ifdef Q38S_TRACE
             const long long tw1 = clock64();
 #endif
@@ -2051,8 +2057,19 @@ uint32_t stream_segments(uint32_t vrows, uint32_t vocab, int device) {
     return s < 1 ? 1 : s;
 }
 
+static uint32_t g_fault_withhold = 0;
+static long long g_fault_wait = 0;
+
+void set_stream_fault(uint32_t withhold, long long wait_cycles) {
+    g_fault_withhold = withhold;
+    g_fault_wait = wait_cycles;
+}
+
 template <int DT>
-static int launch_stream_t(const SampleArgs& a, void* stream) {
+static int launch_stream_t(const SampleArgs& a_in, void* stream) {
+    SampleArgs a = a_in;
+    a.test_withhold = g_fault_withhold;
+    a.test_wait_cycles = g_fault_wait;
     auto kern = stream_kernel<DT>;
     const size_t smem = stream_smem_bytes();
     static bool configured[2][64] = {};

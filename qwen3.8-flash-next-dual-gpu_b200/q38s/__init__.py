@@ -39,7 +39,7 @@ EXPORTS = (
     "q38s_batch_reset", "q38s_batch_states", "q38s_batch_commit_tokens", "q38s_batch_prepare",
     "q38s_batch_commit", "q38s_batch_sample_commit",
     "q38s_mtp_verify", "q38s_shard_topk", "q38s_shard_merge_sample", "q38s_argmax_bf16",
-    "q38s_prepare_noalloc",
+    "q38s_testing_set_fault", "q38s_prepare_noalloc",
 )
 
 
@@ -150,6 +150,7 @@ def lib():
         L.q38s_shard_topk.argtypes = [P, P, u16, u64, u32, P, P]
         L.q38s_shard_merge_sample.argtypes = [P, P, u32, u32, P, P]
         L.q38s_argmax_bf16.argtypes = [P, u32, P, P, i32]
+        L.q38s_testing_set_fault.argtypes = [u32, u64]
         _lib = L
     return _lib
 
