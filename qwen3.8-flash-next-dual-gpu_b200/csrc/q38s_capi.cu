@@ -221,7 +221,7 @@ int create_batch(int device, uint32_t full_vocab, uint32_t col_begin, uint32_t c
         alloc(reinterpret_cast<void**>(&b->d_counts),
               sizeof(uint32_t) * static_cast<size_t>(columns) * rows);
     alloc(reinterpret_cast<void**>(&b->d_scratch),
-          2 * sizeof(uint32_t) * static_cast<size_t>(columns) * rows);  // keys, weights
+          sizeof(uint32_t) * scratch_stride(columns) * rows);  // general-path keys, sums
     b->scratch_rows = rows;
     if (e == cudaSuccess)
         e = cudaMemcpy(b->d_params, params.data(), sizeof(RowParams) * rows,
@@ -277,7 +277,7 @@ SampleArgs base_args(const q38s_batch* b, const void* logits, uint16_t dtype,
     a.counts = b->d_counts;
     a.vrow_state_const = ~0u;
     a.scratch = b->d_scratch;
-    a.scratch_w = reinterpret_cast<float*>(b->d_scratch + static_cast<size_t>(b->vocab) * b->rows);
+    a.scratch_stride = scratch_stride(b->vocab);
     return a;
 }
 
@@ -422,8 +422,8 @@ int q38s_mtp_verify(const q38s_batch* bc, uint32_t row, const void* target, cons
                     "speculative verification needs 0 < top_k <= 1024");
     DeviceGuard g(b->device);
     if (!b->d_mtp_scratch) {
-        cudaError_t e = cudaMalloc(&b->d_mtp_scratch,  // keys, weights
-                                   2 * sizeof(uint32_t) * static_cast<size_t>(b->vocab) * kMtpRows);
+        cudaError_t e = cudaMalloc(&b->d_mtp_scratch,  // general-path keys, sums
+                                   sizeof(uint32_t) * scratch_stride(b->vocab) * kMtpRows);
         if (e == cudaSuccess)
             e = cudaMalloc(&b->d_mtp_tokens, sizeof(int32_t) * kLeaderCap * kMtpRows);
         if (e == cudaSuccess)
@@ -451,7 +451,7 @@ int q38s_mtp_verify(const q38s_batch* bc, uint32_t row, const void* target, cons
     a.dist.n_retained = b->d_mtp_nret;
     a.dist.n_candidates = b->d_mtp_ncand;
     a.scratch = b->d_mtp_scratch;
-    a.scratch_w = reinterpret_cast<float*>(b->d_mtp_scratch + static_cast<size_t>(b->vocab) * kMtpRows);
+    a.scratch_stride = scratch_stride(b->vocab);
     a.mtp = result;
     a.n_draft = n_draft;
     a.draft_tokens = draft_tokens;
@@ -842,12 +842,11 @@ struct NoAllocLayout {  // byte offsets into the static array
     static constexpr size_t params = 0;
     static constexpr size_t state = params + 256;
     static constexpr size_t bitmap = state + 256;  // cleared per call
-    static constexpr size_t keys =
+    static constexpr size_t scratch =  // general-path keys and sums, per row
         bitmap + sizeof(uint32_t) * static_cast<size_t>(kNoAllocBitmapWords) * kNoAllocRows;
-    static constexpr size_t weights =
-        keys + sizeof(uint32_t) * static_cast<size_t>(kNoAllocVocab) * kNoAllocRows;
     static constexpr size_t end =
-        weights + sizeof(float) * static_cast<size_t>(kNoAllocVocab) * kNoAllocRows;
+        scratch + sizeof(uint32_t) * ((static_cast<size_t>(kNoAllocVocab) + 3u) / 4u * 4u +
+                                      kGAuxWords) * kNoAllocRows;
 };
 static_assert(sizeof(RowParams) * kNoAllocRows <= 256, "params slot");
 static_assert(sizeof(RowState) * kNoAllocRows <= 256, "state slot");
@@ -950,8 +949,8 @@ extern "C" int q38s_prepare_noalloc(const void* logits, uint16_t dtype, uint32_t
     a.counts = nullptr;  // no history: every count is zero
     a.vrow_state_const = ~0u;
     a.decisions = decisions;
-    a.scratch = reinterpret_cast<uint32_t*>(base + NoAllocLayout::keys);
-    a.scratch_w = reinterpret_cast<float*>(base + NoAllocLayout::weights);
+    a.scratch = reinterpret_cast<uint32_t*>(base + NoAllocLayout::scratch);
+    a.scratch_stride = scratch_stride(vocabulary);
     a.segs = stream_segments(rows, vocabulary, device);
     const int e = launch_stream(a, stream);
     if (e != cudaSuccess) return cuda_fail(static_cast<cudaError_t>(e), "prepare_noalloc");

@@ -11,7 +11,13 @@ namespace q38s {
 
 constexpr int kThreads = 256;        // threads per CTA of the small kernels
 constexpr int kLeaderCap = 1024;     // candidates of a distribution / shard list
-constexpr uint32_t kMaxGeneralVocab = 1u << 20;  // fixed-point mass headroom
+constexpr uint32_t kMaxGeneralVocab = 1u << 20;  // column radix of the general path
+constexpr uint32_t kGAuxWords = 16384;           // general-path words after a row's keys
+
+// 32-bit words of general-path scratch per virtual row (16-byte aligned rows).
+__host__ __device__ inline uint64_t scratch_stride(uint32_t vocab) {
+    return ((static_cast<uint64_t>(vocab) + 3u) & ~3ull) + kGAuxWords;
+}
 
 // Per-row mutable sampler state: SamplerStateV1 (sampling.h:31-39) minus
 // its constant header words.
@@ -73,10 +79,11 @@ struct SampleArgs {
     q38s_distribution dist;
     q38s_candidate* topk_out;  // kModeShardTopK: vrows * k_out entries
     uint32_t k_out;
-    // general-path scratch: one vocab-sized key array per virtual row, and
-    // one vocab-sized float weight array per virtual row
+    // general-path scratch, scratch_stride 32-bit words per virtual row:
+    // the exact key of every column (padded to a multiple of 4 words), then
+    // kGAuxWords of prefix sums and histograms
     uint32_t* scratch;
-    float* scratch_w;
+    uint64_t scratch_stride;
     // speculative verification, run by the last row to finish
     q38s_mtp_result* mtp;
     uint32_t n_draft;

@@ -61,7 +61,6 @@ constexpr uint32_t kBuf = 2048;                  // candidate buffer (rank keys)
 constexpr uint32_t kFinal = 1024;                // candidates entering the epilogue
 constexpr uint32_t kGather = 1024;               // exact gather of the general path
 constexpr uint32_t kArea = 32768;                // candidate / epilogue work area
-constexpr double kFix = 8796093022208.0;         // 2^43: fixed-point weight unit
 
 constexpr uint32_t kHdrKeys = 64;                // value keys per row in the segments' headers
 
@@ -188,15 +187,6 @@ __device__ uint32_t csum_u32(uint32_t v, Ctl& c) {
     cbar();
     uint32_t r = 0;
     for (int i = 0; i < kCons / 32; ++i) r += c.red_u32[i];
-    return r;
-}
-__device__ uint64_t csum_u64(uint64_t v, Ctl& c) {
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    cbar();
-    if ((threadIdx.x & 31) == 0) c.red_u64[threadIdx.x >> 5] = v;
-    cbar();
-    uint64_t r = 0;
-    for (int i = 0; i < kCons / 32; ++i) r += c.red_u64[i];
     return r;
 }
 // Exclusive prefix sum over the consumers in thread order; *total gets the sum.
@@ -1014,236 +1004,763 @@ __device__ void row_done(const SampleArgs& a, unsigned char* area, Ctl& c) {
 }
 
 // ------------------------------------------------------------ general path
-struct Cut {
-    uint32_t M_key;
-    float M;
-    uint32_t minp_key;
-    bool has_cut;
-    uint32_t cut_key;
-    uint32_t cut_tok;
+// Rows whose kept set the streaming threshold cannot bound (top_k = 0 or
+// top_k > 256 without min-p, or more than kFinal candidates after the cuts).
+// One CTA per row:
+//   P1  the exact value key (sampling.cc:76-92) of every column into global
+//       scratch, and the row maximum M;
+//   K0  the candidate set after min-p and top-k (sampling.cc:94-104 plus
+//       min-p); a top-k cut is located by count, as below;
+//   P2  a histogram of K0 over kGB distance bins: d = fl(M - v) in [0, 64)
+//       in steps of 1/32 (d >= 64 and -inf in the last bin).  The
+//       reference's weight of an element is exp(fl(v - M)) = exp(-d)
+//       (sampling.cc:110-113), so a bin's mass is exp(-b/32) times the sum
+//       of its in-bin weights exp(-(d - b/32)), kept in 2^-40 fixed point
+//       (exact integer sums, independent of thread order).  Bins in order
+//       are the canonical order (value desc); their exclusive prefix counts
+//       and masses go to the row's scratch.
+//   locate  the first K0 element (canonical order: value desc, token asc) at
+//       which the running count, or the running mass, reaches a target: its
+//       bin from the prefixes, then key sub-bins of that bin until at most
+//       kGL elements remain (gathered, sorted, exact double weights summed
+//       in order) or a single key remains (a tie group: the position by
+//       arithmetic, the token by a radix over the columns).
+// Top-p locates top_p * Z (Z = the mass of K0; the quotient-accumulating
+// loop of sampling.cc:119-131 up to rounding); the draw locates
+// uniform01(rng + gamma) * Z_r strictly (sampling.cc:133-145), Z_r being the
+// mass through the top-p cut.  Masses above the final list are exact to
+// about 1e-12 relative; the final list is summed in the reference's order.
+constexpr uint32_t kGB = 2048;              // distance bins, 1/32 wide
+constexpr double kGUnit = 1099511627776.0;  // 2^40: fixed-point unit of in-bin weights
+constexpr uint32_t kGL = kGather;           // largest span gathered and sorted exactly
+// scratch words after a row's keys: prefix counts [kGB + 1] (+1 pad), prefix
+// masses [kGB + 1] (doubles), then the emission's sub-bin counts, one row of
+// kGB per refinement depth
+constexpr uint32_t kAuxPm = kGB + 2;
+constexpr uint32_t kAuxSub = kAuxPm + 2 * (kGB + 1) + 1;
+constexpr uint32_t kEmitDepth = 3;
+static_assert(kAuxSub + kEmitDepth * kGB <= kGAuxWords, "general-path scratch words");
+static_assert(kGB * 12 <= kArea && kGL * 16 + (kGB + 1) * 4 <= kArea, "general-path area");
+
+struct GRow {
+    const uint32_t* keys;  // exact key per column (padded to whole 16-byte groups)
+    uint32_t V, tok0;
+    float M;               // the row maximum
+    uint32_t minp_key;     // smallest key whose weight reaches min_p (0: no min-p)
+    bool has_cut;          // top-k cut: the canonical position (cut_key, cut_col)
+    uint32_t cut_key, cut_col;
 };
 
-__device__ __forceinline__ bool in_k0(const Cut& g, uint32_t key, uint32_t tok) {
+__device__ __forceinline__ bool g_in(const GRow& g, uint32_t key, uint32_t col) {
     if (key < g.minp_key) return false;
     if (!g.has_cut) return true;
-    return key > g.cut_key || (key == g.cut_key && tok <= g.cut_tok);
+    return key > g.cut_key || (key == g.cut_key && col <= g.cut_col);
 }
-// Weight of a key relative to the row maximum M, as the mass-weighted
-// selection stores it: expf(v - M) in single precision (within a few 2^-24
-// relative of the reference's double weights; this path is approximate by
-// construction and its draws count as boundary cases).
-__device__ __forceinline__ float weight_of(uint32_t key, float M) {
-    return expf(__fsub_rn(key_float(key), M));
+// Distance d = fl(M - v) (the negated fl(v - M) of the reference) and its bin.
+__device__ __forceinline__ uint32_t g_bin(const GRow& g, uint32_t key, float& d) {
+    d = __fsub_rn(g.M, key_float(key));
+    const float s = __fmul_rn(d, 32.0f);
+    return s < static_cast<float>(kGB - 1) ? static_cast<uint32_t>(s) : kGB - 1;
 }
-__device__ __forceinline__ uint64_t wfix(float w) {
-    return static_cast<uint64_t>(static_cast<double>(w) * kFix + 0.5);
+// exp(-(d - b/32)) in 2^-40 units (0 for d >= 64, where weights are below
+// 2^-92 of the maximum's): a Taylor series to the sixth power of r < 1/32
+// (truncation below 6e-15).
+__device__ __forceinline__ unsigned long long g_tw(float d, uint32_t b) {
+    if (!(d < 64.0f)) return 0ull;
+    const double r = static_cast<double>(d) - static_cast<double>(b) * 0.03125;
+    double t = 1.0 - r * (1.0 / 6.0);
+    t = 1.0 - r * 0.2 * t;
+    t = 1.0 - r * 0.25 * t;
+    t = 1.0 - r * (1.0 / 3.0) * t;
+    t = 1.0 - r * 0.5 * t;
+    t = 1.0 - r * t;
+    return __double2ull_rn(t * kGUnit);
+}
+// The reference's weight of a key, exp((double)fl(v - M)) (sampling.cc:112).
+__device__ __forceinline__ double g_weight(const GRow& g, uint32_t key) {
+    return exp(static_cast<double>(__fsub_rn(key_float(key), g.M)));
+}
+__device__ __forceinline__ double g_bin_scale(uint32_t b) {
+    return exp(-static_cast<double>(b) * 0.03125);
 }
 
-// Visits every column j < V of the row's scratch arrays, eight per thread
-// per round with the loads issued first (memory-level parallelism for
-// L2-resident arrays); f(j, key, weight, valid) runs a warp-uniform number
-// of rounds (valid is false past the end), so f may use warp collectives.
-// `wts` may be null (weight 0).
+// Exclusive prefix sum of doubles over the consumers in thread order.
+__device__ double cscan_excl_f64(double v, double* total, Ctl& c) {
+    const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    double inc = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= static_cast<uint32_t>(o)) inc += y;
+    }
+    double excl = __shfl_up_sync(0xffffffffu, inc, 1);
+    if (lane == 0) excl = 0.0;
+    cbar();
+    if (lane == 31) c.red_u64[w] = static_cast<uint64_t>(__double_as_longlong(inc));
+    cbar();
+    double before = 0.0, all = 0.0;
+    for (uint32_t i = 0; i < kCons / 32; ++i) {
+        const double x = __longlong_as_double(static_cast<long long>(c.red_u64[i]));
+        if (i < w) before += x;
+        all += x;
+    }
+    *total = all;
+    return before + excl;
+}
+
+// Visits every column j < V with its key, eight 16-byte groups of keys per
+// thread in flight; f(col, key, valid) runs a warp-uniform number of times.
 template <typename F>
-__device__ __forceinline__ void for_keys(const uint32_t* keys, const float* wts, uint32_t V,
-                                         F&& f) {
-    constexpr uint32_t kStep = 8 * kCons;
-    const uint32_t rounds = (V + kStep - 1) / kStep;
-    for (uint32_t b = 0; b < rounds; ++b) {
-        const uint32_t j0 = b * kStep + threadIdx.x;
-        uint32_t kk[8];
-        float ww[8];
+__device__ __forceinline__ void g_for_keys(const GRow& g, F&& f) {
+    constexpr int kIn = 8;
+    const uint32_t nq = (g.V + 3) / 4;
+    const uint4* kq = reinterpret_cast<const uint4*>(g.keys);
+    for (uint32_t base = 0; base < nq; base += kIn * kCons) {
+        uint4 kv[kIn];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t j = j0 + i * kCons;
-            kk[i] = j < V ? keys[j] : 0u;
-            ww[i] = (wts && j < V) ? wts[j] : 0.0f;
+        for (int i = 0; i < kIn; ++i) {
+            const uint32_t q = base + i * kCons + threadIdx.x;
+            kv[i] = q < nq ? __ldcg(kq + q) : make_uint4(0u, 0u, 0u, 0u);
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t j = j0 + i * kCons;
-            f(j, kk[i], ww[i], j < V);
+        for (int i = 0; i < kIn; ++i) {
+            const uint32_t c0 = (base + i * kCons + threadIdx.x) * 4;
+            f(c0, kv[i].x, c0 < g.V);
+            f(c0 + 1, kv[i].y, c0 + 1 < g.V);
+            f(c0 + 2, kv[i].z, c0 + 2 < g.V);
+            f(c0 + 3, kv[i].w, c0 + 3 < g.V);
         }
     }
 }
 
-struct Sel {
-    bool found;
-    uint32_t key;
-    uint32_t token;
-    uint64_t through;  // count or fixed-point mass up to and including the element
-};
-
-// Radix selection over the row's exact keys (global scratch, one per
-// column) restricted to K0 (or to key >= minp_key when !restrict_k0): the
-// first element in canonical order (value desc, token asc) at which the
-// running count (wts == null) or fixed-point mass (wts: the stored weights)
-// reaches tau (>= tau, or > tau when strict).
-// The general path's histograms: per-warp rows of 256 bins (counts, then
-// fixed-point masses) in the work area, which is free while the general
-// path selects.  Every active lane adds its count and mass to its warp's
-// row with shared-memory atomics (exact integer sums); the rows are summed
-// per bin after a pass.  A saved histogram (counts, masses) follows them.
-constexpr uint32_t kRowsW = kCons / 32;
-constexpr uint32_t kSaved = kRowsW * 256 * 12;  // byte offset of the saved histogram
-static_assert(kSaved + 256 * 12 <= kArea, "general-path histograms");
-struct HistRows {
-    uint32_t* hist;            // [kRowsW][256]
-    unsigned long long* mass;  // [kRowsW][256]
-    __device__ explicit HistRows(unsigned char* area)
-        : hist(reinterpret_cast<uint32_t*>(area)),
-          mass(reinterpret_cast<unsigned long long*>(area + kRowsW * 256 * 4)) {}
-    __device__ void clear() {
-        for (uint32_t i = threadIdx.x; i < kRowsW * 256; i += kCons) {
-            hist[i] = 0;
-            mass[i] = 0;
-        }
-    }
-    __device__ void add(uint32_t bin, uint64_t m, bool weighted) {
-        const uint32_t row = (threadIdx.x >> 5) * 256;
-        atomicAdd(&hist[row + bin], 1u);
-        if (weighted) atomicAdd(&mass[row + bin], static_cast<unsigned long long>(m));
-    }
-    __device__ void sum(Ctl& c) {  // bin threadIdx.x over the warps' rows
-        uint32_t h = 0;
-        uint64_t m = 0;
+// P1: the exact key of every column into g.keys (16-byte stores), eight
+// 16-byte groups of logits per thread in flight.  Returns the largest key.
+template <int DT>
+__device__ uint32_t g_keys(const SampleArgs& a, const Row& r, const unsigned char* row,
+                           const uint32_t* pbm, uint32_t* keys, uint32_t V, Ctl& c) {
+    constexpr uint32_t es = DT == Q38S_DTYPE_BF16 ? 2u : 4u;
+    constexpr uint32_t pv = 16u / es;
+    constexpr int kIn = 8;
+    const uint32_t nvec = (V + pv - 1) / pv;
+    uint32_t kmax = 0;
+    for (uint32_t base = 0; base < nvec; base += kIn * kCons) {
+        uint4 w[kIn];
 #pragma unroll
-        for (uint32_t w = 0; w < kRowsW; ++w) {
-            h += hist[w * 256 + threadIdx.x];
-            m += mass[w * 256 + threadIdx.x];
+        for (int i = 0; i < kIn; ++i) {
+            const uint32_t q = base + i * kCons + threadIdx.x;
+            w[i] = q < nvec ? load_vec<DT>(a, row, q * pv, min(pv, V - q * pv))
+                            : make_uint4(0u, 0u, 0u, 0u);
         }
-        c.hist[threadIdx.x] = h;
-        c.hmass[threadIdx.x] = m;
+#pragma unroll
+        for (int i = 0; i < kIn; ++i) {
+            const uint32_t q = base + i * kCons + threadIdx.x;
+            if (q >= nvec) continue;
+            const uint32_t col0 = q * pv;
+            uint32_t pw = 0;  // penalised bits of the 32-column word holding the vector
+            if (r.pen) pw = pbm ? pbm[col0 >> 5] : r.gbm[col0 >> 5];
+            uint32_t k[pv];
+#pragma unroll
+            for (uint32_t e = 0; e < pv; ++e) {
+                const uint32_t col = col0 + e;
+                bool pen = false;
+                uint64_t count = 1;
+                if (r.pen && col < V) {
+                    const uint64_t ex = (!pbm && r.n_extra) ? extra_count(r, a.col_begin + col) : 0u;
+                    pen = ((pw >> (col & 31)) & 1u) || ex != 0;
+                    if (pen && r.freq)
+                        count = (r.counts_row ? r.counts_row[col] : 0u) +
+                                (pbm ? extra_count(r, a.col_begin + col) : ex);
+                }
+                k[e] = col < V ? float_key(transform(vec_elem<DT>(w[i], static_cast<int>(e)), pen,
+                                                     count, r.p))
+                               : 0u;
+                kmax = max(kmax, k[e]);
+            }
+            if (col0 + pv <= V) {
+                uint4* dst = reinterpret_cast<uint4*>(keys + col0);
+                dst[0] = make_uint4(k[0], k[1], k[2], k[3]);
+                if (pv == 8) dst[1] = make_uint4(k[pv == 8 ? 4 : 0], k[pv == 8 ? 5 : 0],
+                                                 k[pv == 8 ? 6 : 0], k[pv == 8 ? 7 : 0]);
+            } else {
+#pragma unroll
+                for (uint32_t e = 0; e < pv; ++e)
+                    if (col0 + e < V) keys[col0 + e] = k[e];
+            }
+        }
     }
+    return cmax_u32(kmax, c);  // its barriers also publish keys[] to the CTA
+}
+
+// P2: histogram of K0 over the distance bins, then each bin's exclusive
+// prefix count (pc) and, when weighted, mass (pm); pc[kGB] / pm[kGB] hold
+// the totals.  Returns |K0|; *Z gets its mass.
+__device__ uint32_t g_level1(const GRow& g, bool weighted, unsigned char* area, uint32_t* pc,
+                             double* pm, double* Z, Ctl& c) {
+    uint32_t* hc = reinterpret_cast<uint32_t*>(area);
+    unsigned long long* hm = reinterpret_cast<unsigned long long*>(area + kGB * 4);
+    cbar();
+    for (uint32_t i = threadIdx.x; i < kGB; i += kCons) {
+        hc[i] = 0;
+        hm[i] = 0;
+    }
+    cbar();
+    g_for_keys(g, [&](uint32_t col, uint32_t key, bool valid) {
+        if (!valid || !g_in(g, key, col)) return;
+        float d;
+        const uint32_t b = g_bin(g, key, d);
+        atomicAdd(&hc[b], 1u);
+        if (weighted) atomicAdd(&hm[b], g_tw(d, b));
+    });
+    cbar();
+    constexpr uint32_t kPer = kGB / kCons;
+    uint32_t lc[kPer], sc = 0;
+    double lm[kPer], sm = 0.0;
+#pragma unroll
+    for (uint32_t j = 0; j < kPer; ++j) {
+        const uint32_t b = threadIdx.x * kPer + j;
+        lc[j] = hc[b];
+        lm[j] = (weighted && hm[b]) ? g_bin_scale(b) * (static_cast<double>(hm[b]) / kGUnit) : 0.0;
+        sc += lc[j];
+        sm += lm[j];
+    }
+    uint32_t tc;
+    uint32_t rc = cscan_excl(sc, &tc, c);
+    double tm = 0.0, rm = 0.0;
+    if (weighted) rm = cscan_excl_f64(sm, &tm, c);
+#pragma unroll
+    for (uint32_t j = 0; j < kPer; ++j) {
+        const uint32_t b = threadIdx.x * kPer + j;
+        pc[b] = rc;
+        rc += lc[j];
+        if (weighted) {
+            pm[b] = rm;
+            rm += lm[j];
+        }
+    }
+    if (threadIdx.x == kCons - 1) {
+        pc[kGB] = tc;
+        if (weighted) pm[kGB] = tm;
+    }
+    cbar();
+    *Z = tm;
+    return tc;
+}
+
+struct GLoc {
+    bool found;
+    uint32_t key, col;  // the element
+    uint32_t idx;       // its canonical position in K0
+    double through;     // the mass (or count) of K0 through it
 };
 
-// l0: a saved first-level histogram (counts, then masses, 256 each) of the
-// same keys, restriction and weights, used instead of the first pass (or
-// null).
-__device__ Sel row_select(const uint32_t* keys, const float* wts, uint32_t V, uint32_t tok0,
-                          const Cut& g0, bool restrict_k0, uint64_t tau, bool strict,
-                          unsigned char* area, const unsigned char* l0, Ctl& c) {
-    const bool weighted = wts != nullptr;
-    HistRows rows(area);
-    Cut g = g0;
-    if (!restrict_k0) g.has_cut = false;
-    uint32_t prefix = 0, mask = 0;
-    uint64_t above = 0;
-    Sel res{false, 0, 0, 0};
-    uint32_t group = 0;
-    for (int level = 0; level < 4; ++level) {
-        const int shift = 24 - 8 * level;
-        cbar();
-        if (level == 0 && l0) {
-            c.hist[threadIdx.x] = reinterpret_cast<const uint32_t*>(l0)[threadIdx.x];
-            c.hmass[threadIdx.x] = reinterpret_cast<const uint64_t*>(l0 + 1024)[threadIdx.x];
+struct GSpan {          // the K0 members with distance bin b1 and key in [lo, hi]
+    uint32_t b1, lo, hi;
+    uint32_t above_cnt;  // K0 elements before the span
+    double above_mass;
+    uint32_t n;          // K0 elements in the span
+};
+
+__device__ __forceinline__ bool g_member(const GRow& g, const GSpan& s, uint32_t key,
+                                         uint32_t col) {
+    if (key < s.lo || key > s.hi || !g_in(g, key, col)) return false;
+    float d;
+    return g_bin(g, key, d) == s.b1;
+}
+
+// Smallest and largest key of the span's members.
+__device__ void g_minmax(const GRow& g, GSpan& s, Ctl& c) {
+    uint32_t lo = 0xffffffffu, hi = 0;
+    g_for_keys(g, [&](uint32_t col, uint32_t key, bool valid) {
+        if (valid && g_member(g, s, key, col)) {
+            lo = min(lo, key);
+            hi = max(hi, key);
+        }
+    });
+    s.lo = cmin_u32(lo, c);
+    s.hi = cmax_u32(hi, c);
+}
+
+// The span's members as rank keys, sorted descending into `sorted`
+// (gathered in `buf`); returns their number (at most kGL).
+__device__ uint32_t g_gather_sorted(const GRow& g, const GSpan& s, uint32_t blo, uint32_t bhi,
+                                    uint64_t* buf, uint64_t* sorted, Ctl& c) {
+    cbar();
+    if (threadIdx.x == 0) c.bc_u32[2] = 0;
+    cbar();
+    g_for_keys(g, [&](uint32_t col, uint32_t key, bool valid) {
+        bool in = valid && key >= s.lo && key <= s.hi && g_in(g, key, col);
+        if (in) {
+            float d;
+            const uint32_t b = g_bin(g, key, d);
+            in = b >= blo && b <= bhi;
+        }
+        warp_push(in, rank_key(key, g.tok0 + col), buf, kGL, &c.bc_u32[2]);
+    });
+    cbar();
+    const uint32_t n = min(c.bc_u32[2], kGL);
+    sort_desc(buf, n, sorted);
+    return n;
+}
+
+// The located element inside a span of at most kGL members: exact weights
+// summed in canonical order from the mass above the span.
+__device__ GLoc g_final(const GRow& g, const GSpan& s, bool mass, double tau, bool strict,
+                        unsigned char* area, Ctl& c) {
+    uint64_t* buf = reinterpret_cast<uint64_t*>(area);
+    uint64_t* lk = reinterpret_cast<uint64_t*>(area + kGL * 8);
+    const uint32_t n = g_gather_sorted(g, s, s.b1, s.b1, buf, lk, c);
+    GLoc res{false, 0, 0, 0, 0.0};
+    if (n == 0) return res;
+    if (threadIdx.x < 32) {
+        const uint32_t lane = threadIdx.x;
+        uint32_t sel = n - 1;
+        double through = 0.0;
+        if (!mass) {
+            const double pos = tau - static_cast<double>(s.above_cnt) - 1.0;
+            sel = pos <= 0.0 ? 0u : min(n - 1, static_cast<uint32_t>(pos));
+            through = static_cast<double>(s.above_cnt + sel + 1);
         } else {
-            rows.clear();
-            cbar();
-            for_keys(keys, wts, V, [&](uint32_t j, uint32_t key, float w, bool valid) {
-                if (valid && (key & mask) == prefix && in_k0(g, key, tok0 + j))
-                    rows.add((key >> shift) & 255u, weighted ? wfix(w) : 0ull, weighted);
-            });
-            cbar();
-            rows.sum(c);
-        }
-        cbar();
-        if (threadIdx.x == 0) {
-            uint64_t acc = above;
-            int hit = -1;
-            for (int d = 255; d >= 0; --d) {
-                if (c.hist[d] == 0) continue;
-                const uint64_t nxt = acc + (weighted ? c.hmass[d] : c.hist[d]);
-                if (strict ? (nxt > tau) : (nxt >= tau)) {
-                    hit = d;
-                    break;
+            double base = s.above_mass;
+            bool hit = false;
+            for (uint32_t i0 = 0; i0 < n && !hit; i0 += 32) {
+                const uint32_t i = i0 + lane;
+                const double w = i < n ? g_weight(g, static_cast<uint32_t>(lk[i] >> 32)) : 0.0;
+                double inc = w;
+                for (int o = 1; o < 32; o <<= 1) {
+                    const double y = __shfl_up_sync(0xffffffffu, inc, o);
+                    if (lane >= static_cast<uint32_t>(o)) inc += y;
                 }
-                acc = nxt;
-            }
-            c.bc_u32[0] = static_cast<uint32_t>(hit);
-            c.bc_u32[1] = hit >= 0 ? c.hist[hit] : 0u;
-            c.bc_u64[0] = acc;
-        }
-        cbar();
-        const int hit = static_cast<int>(c.bc_u32[0]);
-        if (hit < 0) return res;
-        group = c.bc_u32[1];
-        above = c.bc_u64[0];
-        prefix |= static_cast<uint32_t>(hit) << shift;
-        mask |= 255u << shift;
-    }
-    // position j inside the tie group {key == prefix} (token order)
-    const uint32_t key = prefix;
-    uint64_t j, per = 1;
-    if (weighted) {
-        per = wfix(weight_of(key, g.M));
-        if (per == 0) {
-            j = 0;
-        } else if (strict) {
-            j = (tau - above) / per;
-        } else {
-            const uint64_t need = tau > above ? tau - above : 0;
-            j = need == 0 ? 0 : (need + per - 1) / per - 1;
-        }
-    } else {
-        j = tau > above ? tau - above - 1 : 0;
-    }
-    if (j >= group) j = group - 1;
-    // the j-th smallest token of the group: a single member is found in one
-    // pass, larger groups by a radix over the token bits
-    uint32_t tprefix = 0;
-    if (group == 1) {
-        cbar();
-        for_keys(keys, nullptr, V, [&](uint32_t x, uint32_t k2, float, bool valid) {
-            if (valid && k2 == key && in_k0(g, key, tok0 + x)) c.bc_u32[3] = tok0 + x;
-        });
-        cbar();
-        tprefix = c.bc_u32[3];
-    } else {
-        uint32_t tmask = 0, need = static_cast<uint32_t>(j);
-        for (int level = 0; level < 4; ++level) {
-            const int shift = 24 - 8 * level;
-            cbar();
-            rows.clear();
-            cbar();
-            for_keys(keys, nullptr, V, [&](uint32_t x, uint32_t k2, float, bool valid) {
-                const uint32_t tok = tok0 + x;
-                if (valid && k2 == key && (tok & tmask) == tprefix && in_k0(g, key, tok))
-                    rows.add((tok >> shift) & 255u, 0ull, false);
-            });
-            cbar();
-            rows.sum(c);
-            cbar();
-            if (threadIdx.x == 0) {
-                uint32_t left = need, d = 0;
-                for (; d < 255; ++d) {
-                    if (left < c.hist[d]) break;
-                    left -= c.hist[d];
+                const double S = base + inc;
+                const uint32_t b = __ballot_sync(0xffffffffu,
+                                                 i < n && (strict ? (S > tau) : (S >= tau)));
+                if (b) {
+                    const uint32_t f = __ffs(b) - 1;
+                    sel = i0 + f;
+                    through = __shfl_sync(0xffffffffu, S, f);
+                    hit = true;
+                } else {
+                    base = __shfl_sync(0xffffffffu, S, 31);
+                    through = base;  // no element reaches the target: the last one
                 }
-                c.bc_u32[0] = d;
-                c.bc_u32[1] = left;
             }
-            cbar();
-            tprefix |= c.bc_u32[0] << shift;
-            tmask |= 255u << shift;
-            need = c.bc_u32[1];
+        }
+        if (lane == 0) {
+            c.bc_u32[0] = sel;
+            c.bc_u64[0] = static_cast<uint64_t>(__double_as_longlong(through));
         }
     }
+    cbar();
+    const uint32_t sel = c.bc_u32[0];
     res.found = true;
-    res.key = key;
-    res.token = tprefix;
-    res.through = above + (j + 1) * per;
+    res.key = static_cast<uint32_t>(lk[sel] >> 32);
+    res.col = rank_token(lk[sel]) - g.tok0;
+    res.idx = s.above_cnt + sel;
+    res.through = __longlong_as_double(static_cast<long long>(c.bc_u64[0]));
+    cbar();
     return res;
 }
 
+// The j-th smallest column among the K0 members holding `key`: a radix over
+// the column bits, 11 then 9 bits (columns < 2^20).
+__device__ uint32_t g_tie_col(const GRow& g, uint32_t key, uint32_t j, unsigned char* area,
+                              Ctl& c) {
+    uint32_t* h = reinterpret_cast<uint32_t*>(area);
+    uint32_t prefix = 0, need = j;
+    for (int level = 0; level < 2; ++level) {
+        const uint32_t nb = level == 0 ? 2048u : 512u;
+        cbar();
+        for (uint32_t i = threadIdx.x; i < nb; i += kCons) h[i] = 0;
+        cbar();
+        g_for_keys(g, [&](uint32_t col, uint32_t k, bool valid) {
+            if (valid && k == key && g_in(g, k, col) && (level == 0 || (col >> 9) == prefix))
+                atomicAdd(&h[level == 0 ? (col >> 9) : (col & 511u)], 1u);
+        });
+        cbar();
+        if (threadIdx.x == 0) {
+            uint32_t left = need, d = 0;
+            for (; d < nb - 1; ++d) {
+                if (left < h[d]) break;
+                left -= h[d];
+            }
+            c.bc_u32[0] = d;
+            c.bc_u32[1] = left;
+        }
+        cbar();
+        if (level == 0) prefix = c.bc_u32[0];
+        else prefix = (prefix << 9) | c.bc_u32[0];
+        need = c.bc_u32[1];
+    }
+    return prefix;
+}
+
+// The located element in a tie group (a span holding one key).
+__device__ GLoc g_tie(const GRow& g, const GSpan& s, bool mass, double tau, bool strict,
+                      unsigned char* area, Ctl& c) {
+    const uint32_t key = s.lo;
+    const double w = g_weight(g, key);
+    double j;
+    if (!mass) j = tau - static_cast<double>(s.above_cnt) - 1.0;
+    else if (!(w > 0.0)) j = static_cast<double>(s.n) - 1.0;
+    else if (strict) j = floor((tau - s.above_mass) / w);
+    else j = ceil((tau - s.above_mass) / w) - 1.0;
+    const uint32_t jj = j <= 0.0 ? 0u : (j >= static_cast<double>(s.n - 1) ? s.n - 1
+                                                                          : static_cast<uint32_t>(j));
+    GLoc res;
+    res.found = true;
+    res.key = key;
+    res.col = g_tie_col(g, key, jj, area, c);
+    res.idx = s.above_cnt + jj;
+    res.through = mass ? s.above_mass + static_cast<double>(jj + 1) * w
+                       : static_cast<double>(s.above_cnt + jj + 1);
+    return res;
+}
+
+// First K0 element at which the running count (mass false: tau an integer
+// count) or mass reaches tau (>= tau, or > tau when strict).
+__device__ GLoc g_locate(const GRow& g, const uint32_t* pc, const double* pm, bool mass,
+                         double tau, bool strict, unsigned char* area, Ctl& c) {
+    constexpr uint32_t kPer = kGB / kCons;
+    // the bin: first b whose running total through it reaches tau
+    uint32_t first = 0xffffffffu;
+#pragma unroll
+    for (uint32_t j = 0; j < kPer; ++j) {
+        const uint32_t b = threadIdx.x * kPer + j;
+        const bool hit = mass ? (strict ? __ldcg(&pm[b + 1]) > tau : __ldcg(&pm[b + 1]) >= tau)
+                              : static_cast<double>(__ldcg(&pc[b + 1])) >= tau;
+        if (hit && first == 0xffffffffu && __ldcg(&pc[b + 1]) > __ldcg(&pc[b])) first = b;
+    }
+    first = cmin_u32(first, c);
+    if (first == 0xffffffffu) {  // rounding: the target lies past the last bin
+        uint32_t last = 0;
+        for (uint32_t j = 0; j < kPer; ++j) {
+            const uint32_t b = threadIdx.x * kPer + j;
+            if (__ldcg(&pc[b + 1]) > __ldcg(&pc[b])) last = b + 1;
+        }
+        last = cmax_u32(last, c);
+        if (last == 0) return GLoc{false, 0, 0, 0, 0.0};
+        first = last - 1;
+    }
+    GSpan s;
+    s.b1 = first;
+    s.lo = 0;
+    s.hi = 0xffffffffu;
+    s.above_cnt = __ldcg(&pc[first]);
+    s.above_mass = mass ? __ldcg(&pm[first]) : 0.0;
+    s.n = __ldcg(&pc[first + 1]) - s.above_cnt;
+    const double scale = g_bin_scale(first);
+    bool bounded = false;
+    for (int level = 0; level < 6; ++level) {
+        if (s.n <= kGL) return g_final(g, s, mass, tau, strict, area, c);
+        if (!bounded) {
+            g_minmax(g, s, c);
+            bounded = true;
+        }
+        if (s.lo == s.hi) return g_tie(g, s, mass, tau, strict, area, c);
+        // key sub-bins of the span, highest keys first
+        const uint32_t span = s.hi - s.lo;
+        const int sh = span > kGB - 1 ? (32 - __clz(span)) - 11 : 0;
+        const uint32_t top = span >> sh;
+        uint32_t* hc = reinterpret_cast<uint32_t*>(area);
+        unsigned long long* hm = reinterpret_cast<unsigned long long*>(area + kGB * 4);
+        cbar();
+        for (uint32_t i = threadIdx.x; i < kGB; i += kCons) {
+            hc[i] = 0;
+            hm[i] = 0;
+        }
+        cbar();
+        g_for_keys(g, [&](uint32_t col, uint32_t key, bool valid) {
+            if (!valid || !g_member(g, s, key, col)) return;
+            const uint32_t sb = top - ((key - s.lo) >> sh);
+            atomicAdd(&hc[sb], 1u);
+            if (mass) {
+                float d;
+                g_bin(g, key, d);
+                atomicAdd(&hm[sb], g_tw(d, s.b1));
+            }
+        });
+        cbar();
+        uint32_t lc[kPer], sc = 0;
+        double lm[kPer], sm = 0.0;
+#pragma unroll
+        for (uint32_t j = 0; j < kPer; ++j) {
+            const uint32_t b = threadIdx.x * kPer + j;
+            lc[j] = hc[b];
+            lm[j] = mass ? scale * (static_cast<double>(hm[b]) / kGUnit) : 0.0;
+            sc += lc[j];
+            sm += lm[j];
+        }
+        uint32_t tc;
+        const uint32_t rc0 = cscan_excl(sc, &tc, c);
+        double tm = 0.0, rm0 = 0.0;
+        if (mass) rm0 = cscan_excl_f64(sm, &tm, c);
+        uint32_t hit = 0xffffffffu, last = 0;
+        {
+            uint32_t rc = rc0;
+            double rm = rm0;
+#pragma unroll
+            for (uint32_t j = 0; j < kPer; ++j) {
+                const uint32_t b = threadIdx.x * kPer + j;
+                if (lc[j]) {
+                    last = b + 1;
+                    const bool h = mass ? (strict ? s.above_mass + rm + lm[j] > tau
+                                                  : s.above_mass + rm + lm[j] >= tau)
+                                        : static_cast<double>(s.above_cnt + rc + lc[j]) >= tau;
+                    if (h && hit == 0xffffffffu) hit = b;
+                }
+                rc += lc[j];
+                rm += lm[j];
+            }
+        }
+        const uint32_t fh = cmin_u32(hit, c);
+        const uint32_t fl = cmax_u32(last, c);
+        const uint32_t sb = fh != 0xffffffffu ? fh : fl - 1;  // rounding: the last non-empty
+        // the owner of sub-bin sb publishes the count and mass before it
+        if (threadIdx.x == sb / kPer) {
+            uint32_t rc = rc0;
+            double rm = rm0;
+            uint32_t own = 0;
+#pragma unroll
+            for (uint32_t j = 0; j < kPer; ++j) {
+                if (j < sb % kPer) {
+                    rc += lc[j];
+                    rm += lm[j];
+                } else if (j == sb % kPer) {
+                    own = lc[j];
+                }
+            }
+            c.bc_u32[0] = rc;
+            c.bc_u64[0] = static_cast<uint64_t>(__double_as_longlong(rm));
+            c.bc_u32[1] = own;
+        }
+        cbar();
+        const uint32_t lo2 = s.lo + ((top - sb) << sh);
+        const uint32_t hi2 = sh ? min(s.hi, lo2 + ((1u << sh) - 1u)) : lo2;
+        s.above_cnt += c.bc_u32[0];
+        if (mass) s.above_mass += __longlong_as_double(static_cast<long long>(c.bc_u64[0]));
+        s.n = c.bc_u32[1];
+        s.lo = lo2;
+        s.hi = hi2;
+        cbar();
+    }
+    return g_final(g, s, mass, tau, strict, area, c);
+}
+
+// ---- distribution output of a general row: K0's first n_emit members in
+// canonical order with their values, and w_i / Z_r for the first r_cnt.
+struct GOut {
+    size_t base;      // row offset in the distribution arrays
+    uint32_t n_emit;
+    uint32_t r_cnt;
+    double Zr;
+};
+
+__device__ void g_write_list(const SampleArgs& a, const GRow& g, const GOut& o, const uint64_t* lk,
+                             uint32_t n, uint32_t pos) {
+    for (uint32_t i = threadIdx.x; i < n; i += kCons) {
+        const uint32_t p = pos + i;
+        if (p >= o.n_emit) break;
+        const uint32_t key = static_cast<uint32_t>(lk[i] >> 32);
+        if (a.dist.tokens) a.dist.tokens[o.base + p] = static_cast<int32_t>(rank_token(lk[i]));
+        if (a.dist.values) a.dist.values[o.base + p] = key_float(key);
+        if (a.dist.probs) a.dist.probs[o.base + p] = p < o.r_cnt ? g_weight(g, key) / o.Zr : 0.0;
+    }
+    cbar();
+}
+
+// The K0 members holding `key` in column order (a tie group), at pos.
+__device__ void g_write_tie(const SampleArgs& a, const GRow& g, const GOut& o, uint32_t key,
+                            uint32_t pos, Ctl& c) {
+    const float val = key_float(key);
+    const double w = g_weight(g, key);
+    const uint4* kq = reinterpret_cast<const uint4*>(g.keys);
+    for (uint32_t c0 = 0; c0 < g.V && pos < o.n_emit; c0 += 16 * kCons) {
+        const uint32_t my0 = c0 + threadIdx.x * 16;  // 16 consecutive columns per thread
+        uint32_t flags = 0;
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) {
+            const uint32_t cq = my0 + 4 * q;
+            if (cq < g.V) {
+                const uint4 kv = __ldcg(kq + cq / 4);
+                const uint32_t kk[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+                for (uint32_t e = 0; e < 4; ++e)
+                    if (cq + e < g.V && kk[e] == key && g_in(g, key, cq + e))
+                        flags |= 1u << (4 * q + e);
+            }
+        }
+        uint32_t tot;
+        uint32_t off = cscan_excl(__popc(flags), &tot, c);
+        while (flags) {
+            const uint32_t e = __ffs(flags) - 1;
+            flags &= flags - 1;
+            const uint32_t p = pos + off++;
+            if (p < o.n_emit) {
+                if (a.dist.tokens) a.dist.tokens[o.base + p] = static_cast<int32_t>(g.tok0 + my0 + e);
+                if (a.dist.values) a.dist.values[o.base + p] = val;
+                if (a.dist.probs) a.dist.probs[o.base + p] = p < o.r_cnt ? w / o.Zr : 0.0;
+            }
+        }
+        pos += tot;
+    }
+    cbar();
+}
+
+// Counts of the key sub-bins of a span (highest keys first) into h.
+__device__ void g_subcount(const GRow& g, const GSpan& s, int sh, uint32_t top, uint32_t* h) {
+    cbar();
+    for (uint32_t i = threadIdx.x; i < kGB; i += kCons) h[i] = 0;
+    cbar();
+    g_for_keys(g, [&](uint32_t col, uint32_t key, bool valid) {
+        if (valid && g_member(g, s, key, col)) atomicAdd(&h[top - ((key - s.lo) >> sh)], 1u);
+    });
+    cbar();
+}
+
+// A distance bin of more than kGL members: its key sub-bins depth first
+// (sub-bin counts of the open levels in scratch, the current one in shared
+// memory), groups of consecutive small sub-bins gathered and sorted, single
+// keys written as tie groups.
+__device__ void g_emit_big(const SampleArgs& a, const GRow& g, const GOut& o, GSpan root,
+                           uint32_t pos, uint32_t* subh, unsigned char* area, Ctl& c) {
+    uint64_t* buf = reinterpret_cast<uint64_t*>(area);
+    uint64_t* lk = reinterpret_cast<uint64_t*>(area + kGL * 8);
+    uint32_t* hs = reinterpret_cast<uint32_t*>(area + kArea - kGB * 4);
+    struct Frame {
+        uint32_t lo, hi, top, sb, pos;
+        int sh;
+    };
+    Frame st[kEmitDepth];
+    int d = 0;
+    auto open = [&](int depth, uint32_t lo, uint32_t hi, uint32_t p) {
+        Frame& f = st[depth];
+        f.lo = lo;
+        f.hi = hi;
+        const uint32_t span = hi - lo;
+        f.sh = span > kGB - 1 ? (32 - __clz(span)) - 11 : 0;
+        f.top = span >> f.sh;
+        f.sb = 0;
+        f.pos = p;
+        GSpan s = root;
+        s.lo = lo;
+        s.hi = hi;
+        g_subcount(g, s, f.sh, f.top, hs);
+        for (uint32_t i = threadIdx.x; i < kGB; i += kCons) subh[depth * kGB + i] = hs[i];
+        cbar();
+    };
+    if (root.lo == root.hi) {
+        g_write_tie(a, g, o, root.lo, pos, c);
+        return;
+    }
+    open(0, root.lo, root.hi, pos);
+    while (d >= 0) {
+        Frame& f = st[d];
+        bool descended = false;
+        while (f.sb <= f.top && f.pos < o.n_emit) {
+            const uint32_t cnt = hs[f.sb];
+            if (cnt == 0) {
+                ++f.sb;
+                continue;
+            }
+            const uint32_t lo2 = f.lo + ((f.top - f.sb) << f.sh);
+            const uint32_t hi2 = f.sh ? min(f.hi, lo2 + ((1u << f.sh) - 1u)) : lo2;
+            if (cnt > kGL) {
+                if (lo2 == hi2 || d + 1 >= static_cast<int>(kEmitDepth)) {
+                    g_write_tie(a, g, o, lo2, f.pos, c);
+                    f.pos += cnt;
+                    ++f.sb;
+                    continue;
+                }
+                const uint32_t p = f.pos;
+                f.pos += cnt;
+                ++f.sb;
+                open(d + 1, lo2, hi2, p);
+                ++d;
+                descended = true;
+                break;
+            }
+            // consecutive sub-bins holding at most kGL members in all
+            uint32_t e = f.sb + 1, tot = cnt;
+            while (e <= f.top && tot + hs[e] <= kGL) tot += hs[e++];
+            GSpan s = root;
+            s.lo = f.lo + ((f.top - (e - 1)) << f.sh);
+            s.hi = hi2;
+            const uint32_t n = g_gather_sorted(g, s, root.b1, root.b1, buf, lk, c);
+            g_write_list(a, g, o, lk, n, f.pos);
+            f.pos += n;
+            f.sb = e;
+        }
+        if (descended) continue;
+        --d;
+        if (d >= 0) {  // back to the parent's sub-bin counts
+            cbar();
+            for (uint32_t i = threadIdx.x; i < kGB; i += kCons) hs[i] = __ldcg(&subh[d * kGB + i]);
+            cbar();
+        }
+    }
+}
+
+__device__ void g_emit(const SampleArgs& a, const Row& r, const GRow& g, const uint32_t* pc,
+                       uint32_t* subh, uint32_t n0, uint32_t r_cnt, double Zr, unsigned char* area,
+                       Ctl& c) {
+    uint64_t* buf = reinterpret_cast<uint64_t*>(area);
+    uint64_t* lk = reinterpret_cast<uint64_t*>(area + kGL * 8);
+    uint32_t* bcnt = reinterpret_cast<uint32_t*>(area + kGL * 16);  // level-1 counts
+    GOut o;
+    o.base = static_cast<size_t>(r.v) * a.dist.capacity;
+    o.n_emit = min(n0, a.dist.capacity);
+    o.r_cnt = r_cnt;
+    o.Zr = Zr;
+    cbar();
+    for (uint32_t b = threadIdx.x; b < kGB; b += kCons) bcnt[b] = __ldcg(&pc[b + 1]) - __ldcg(&pc[b]);
+    cbar();
+    uint32_t pos = 0, b = 0;
+    while (b < kGB && pos < o.n_emit) {
+        const uint32_t cnt = bcnt[b];
+        if (cnt == 0) {
+            ++b;
+            continue;
+        }
+        GSpan s;
+        s.b1 = b;
+        s.lo = 0;
+        s.hi = 0xffffffffu;
+        s.above_cnt = pos;
+        s.above_mass = 0.0;
+        s.n = cnt;
+        if (cnt > kGL) {
+            g_minmax(g, s, c);
+            g_emit_big(a, g, o, s, pos, subh, area, c);
+            // the level-1 counts live beside the sub-bin counts: reload them
+            cbar();
+            for (uint32_t i = threadIdx.x; i < kGB; i += kCons)
+                bcnt[i] = __ldcg(&pc[i + 1]) - __ldcg(&pc[i]);
+            cbar();
+            pos += cnt;
+            ++b;
+            continue;
+        }
+        uint32_t e = b + 1, tot = cnt;
+        while (e < kGB && tot + bcnt[e] <= kGL) tot += bcnt[e++];
+        const uint32_t n = g_gather_sorted(g, s, b, e - 1, buf, lk, c);
+        g_write_list(a, g, o, lk, n, pos);
+        pos += n;
+        b = e;
+    }
+}
+
+// Out of line: the general path's register needs stay out of the stream loop.
 template <int DT>
-__device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* area, Ctl& c) {
+__device__ __noinline__ void general_row(const SampleArgs& a, const Row& r, unsigned char* area,
+                                         Ctl& c) {
     const uint32_t V = a.vocab;
     const uint32_t tok0 = a.col_begin;
-    uint32_t* keys = a.scratch + static_cast<size_t>(r.v) * V;
-    float* wts = a.scratch_w + static_cast<size_t>(r.v) * V;
+    uint32_t* keys = a.scratch + static_cast<size_t>(r.v) * a.scratch_stride;
+    uint32_t* aux = keys + ((V + 3u) & ~3u);
+    uint32_t* pc = aux;
+    double* pm = reinterpret_cast<double*>(aux + kAuxPm);
+    uint32_t* subh = aux + kAuxSub;
     const unsigned char* row = row_ptr<DT>(a, r.v);
-    // this call's penalised columns in shared memory when they fit
+    // this call's penalised columns (bitmap plus additional tokens) in
+    // shared memory when they fit
     const uint32_t words = (V + 31) / 32;
     const uint32_t* pbm = nullptr;
     if (r.pen && words * 4 <= kArea) {
@@ -1258,59 +1775,29 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         cbar();
         pbm = sbm;
     }
-    // G0: exact key of every column (eight loads in flight per thread)
-    uint32_t kmax = 0;
-    constexpr uint32_t kStep = 8 * kCons;
-    for (uint32_t b = 0; b < (V + kStep - 1) / kStep; ++b) {
-        float xs[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t j = b * kStep + threadIdx.x + i * kCons;
-            xs[i] = j < V ? load_elem<DT>(row, j) : 0.0f;
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t j = b * kStep + threadIdx.x + i * kCons;
-            if (j >= V) break;
-            bool penalized = false;
-            uint64_t count = 1;
-            if (r.pen) {
-                if (pbm) {
-                    penalized = (pbm[j >> 5] >> (j & 31)) & 1u;
-                    if (penalized && r.freq)
-                        count = (r.counts_row ? r.counts_row[j] : 0u) + extra_count(r, tok0 + j);
-                } else {
-                    const uint64_t ex = extra_count(r, tok0 + j);
-                    penalized = ((r.gbm[j >> 5] >> (j & 31)) & 1u) || ex;
-                    if (penalized && r.freq) count = (r.counts_row ? r.counts_row[j] : 0u) + ex;
-                }
-            }
-            const uint32_t k = float_key(exact_value(xs[i], penalized, count, r.p));
-            keys[j] = k;
-            kmax = max(kmax, k);
-        }
-    }
+    GRow g;
+    g.keys = keys;
+    g.V = V;
+    g.tok0 = tok0;
+    const uint32_t M_key = g_keys<DT>(a, r, row, pbm, keys, V, c);
     Q38S_TT(r.v, 6);
-    Cut g;
-    g.M_key = cmax_u32(kmax, c);  // its barriers also publish keys[] to the CTA
-    g.M = key_float(g.M_key);
+    g.M = key_float(M_key);
+    g.minp_key = 0;
     g.has_cut = false;
     g.cut_key = 0;
-    g.cut_tok = 0;
-    g.minp_key = 0;
-    if (a.mode != kModeShardTopK && (g.M_key <= kNegInfKey || isinf(g.M))) {
+    g.cut_col = 0;
+    if (a.mode != kModeShardTopK && (M_key <= kNegInfKey || isinf(g.M))) {
         row_error(a, r, Q38S_ROW_NO_FINITE);
         return;
     }
-    // G1: smallest key whose weight reaches min_p
-    if (r.minp) {
+    // smallest key whose weight reaches min_p
+    if (r.minp && M_key > kNegInfKey && !isinf(g.M)) {
         if (threadIdx.x == 0) {
             const double floor_w = static_cast<double>(r.p.min_p);
-            uint32_t lo = kNegInfKey, hi = g.M_key;  // weight(M) = 1 >= min_p
+            uint32_t lo = kNegInfKey, hi = M_key;  // weight(M) = 1 >= min_p
             while (lo < hi) {
                 const uint32_t mid = lo + (hi - lo) / 2;
-                const double w = exp(static_cast<double>(__fsub_rn(key_float(mid), g.M)));
-                if (w >= floor_w) hi = mid;
+                if (g_weight(g, mid) >= floor_w) hi = mid;
                 else lo = mid + 1;
             }
             c.bc_u32[3] = hi;
@@ -1318,92 +1805,85 @@ __device__ void general_row(const SampleArgs& a, const Row& r, unsigned char* ar
         cbar();
         g.minp_key = c.bc_u32[3];
     }
-    // G2: the kept set K0 = top-k of {key >= minp_key}
-    uint32_t cnt = 0;
-    for_keys(keys, nullptr, V, [&](uint32_t, uint32_t key, float, bool valid) {
-        cnt += valid && key >= g.minp_key;
-    });
-    const uint32_t c_minp = csum_u32(cnt, c);
-    const uint32_t n0 = r.k_eff ? min(r.k_eff, c_minp) : c_minp;
-    if (n0 < c_minp) {
-        const Sel cut = row_select(keys, nullptr, V, tok0, g, false, n0, false, area, nullptr, c);
-        g.has_cut = true;
-        g.cut_key = cut.key;
-        g.cut_tok = cut.token;
+    // |K0| and the top-k cut
+    uint32_t n0 = V;
+    if (r.minp || r.k_eff) {
+        uint32_t cnt = 0;
+        g_for_keys(g, [&](uint32_t, uint32_t key, bool valid) {
+            cnt += valid && key >= g.minp_key;
+        });
+        n0 = csum_u32(cnt, c);
+        if (r.k_eff && r.k_eff < n0) {
+            double unused;
+            g_level1(g, false, area, pc, pm, &unused, c);
+            const GLoc cut = g_locate(g, pc, pm, false, static_cast<double>(r.k_eff), false, area, c);
+            g.has_cut = true;
+            g.cut_key = cut.key;
+            g.cut_col = cut.col;
+            n0 = r.k_eff;
+        }
     }
     Q38S_TT(r.v, 10);
-    if (n0 <= kGather) {
-        // G3: gather K0, sort, finish exactly
-        uint64_t* gk = reinterpret_cast<uint64_t*>(area + kGather * 8);  // unsorted
-        uint64_t* lk = reinterpret_cast<uint64_t*>(area);                 // sorted
-        cbar();
-        if (threadIdx.x == 0) c.bc_u32[2] = 0;
-        cbar();
-        for_keys(keys, nullptr, V, [&](uint32_t j, uint32_t k, float, bool valid) {
-            const bool act = valid && in_k0(g, k, tok0 + j);
-            warp_push(act, rank_key(k, tok0 + j), gk, kGather, &c.bc_u32[2]);
-        });
-        cbar();
-        const uint32_t m = min(c.bc_u32[2], kGather);
-        sort_desc(gk, m, lk);
-        double* w = reinterpret_cast<double*>(area + kGather * 8);
-        double* S = reinterpret_cast<double*>(area + kGather * 16);
-        double* q = reinterpret_cast<double*>(area + kGather * 24);
+    if (n0 <= kGL) {
+        // gather K0, sort, and the exact epilogue of the fast path
+        uint64_t* buf = reinterpret_cast<uint64_t*>(area);
+        uint64_t* lk = reinterpret_cast<uint64_t*>(area + kGL * 8);
+        GSpan s;
+        s.b1 = 0;
+        s.lo = 0;
+        s.hi = 0xffffffffu;
+        const uint32_t m = g_gather_sorted(g, s, 0, kGB - 1, buf, lk, c);
+        double* w = reinterpret_cast<double*>(area);  // over the dead gather buffer
+        double* S = reinterpret_cast<double*>(area + kGL * 16);
+        double* q = reinterpret_cast<double*>(area + kGL * 24);
         row_output(a, r, lk, m, w, S, q, c);
         return;
     }
-    // G4: large kept set: weights once (float), then fixed-point masses
-    // (2^-43 units) locate the top-p cut and the draw
-    // (and the first-level histogram of both weighted selections below: the
-    // same keys, restriction and weights)
-    uint64_t part = 0;
-    HistRows rows(area);
-    cbar();
-    rows.clear();
-    cbar();
-    for_keys(keys, nullptr, V, [&](uint32_t j, uint32_t k, float, bool valid) {
-        if (!valid) return;
-        const bool in = in_k0(g, k, tok0 + j);
-        const float w = in ? weight_of(k, g.M) : 0.0f;
-        wts[j] = w;
-        part += wfix(w);
-        if (in) rows.add(k >> 24, wfix(w), true);
-    });
-    const uint64_t Z = csum_u64(part, c);  // its barriers also publish wts[] and the rows
-    rows.sum(c);
-    reinterpret_cast<uint32_t*>(area + kSaved)[threadIdx.x] = c.hist[threadIdx.x];
-    reinterpret_cast<uint64_t*>(area + kSaved + 1024)[threadIdx.x] = c.hmass[threadIdx.x];
-    cbar();
+    if (a.mode == kModeShardTopK) {  // candidate lists hold at most kLeaderCap
+        row_error(a, r, Q38S_ROW_NORMALIZATION);
+        return;
+    }
+    double Z = 0.0;
+    g_level1(g, true, area, pc, pm, &Z, c);
     Q38S_TT(r.v, 13);
-    int32_t status = Q38S_ROW_OK;
-    int32_t token = -1;
-    uint64_t Zr = Z;
-    Sel cutp{false, 0, 0, 0};
-    if (Z == 0) status = Q38S_ROW_NORMALIZATION;
-    if (status == Q38S_ROW_OK && r.p.top_p < 1.0f) {
-        const uint64_t tau = static_cast<uint64_t>(static_cast<double>(r.p.top_p) *
-                                                   static_cast<double>(Z));
-        cutp = row_select(keys, wts, V, tok0, g, true, tau, false, area, area + kSaved, c);
-        if (cutp.found) Zr = cutp.through;
+    if (!(Z > 0.0) || !isfinite(Z)) {
+        row_error(a, r, Q38S_ROW_NORMALIZATION);
+        return;
+    }
+    uint32_t r_cnt = n0;
+    double Zr = Z;
+    GLoc cut{false, 0, 0, 0, 0.0};
+    if (r.p.top_p < 1.0f) {
+        cut = g_locate(g, pc, pm, true, static_cast<double>(r.p.top_p) * Z, false, area, c);
+        if (cut.found) {
+            r_cnt = cut.idx + 1;
+            Zr = cut.through;
+        }
     }
     Q38S_TT(r.v, 14);
-    double draw_d = 0.0;
-    if (status == Q38S_ROW_OK) {
-        const double u = uniform01(r.rng_before + kGamma);
-        const uint64_t draw = static_cast<uint64_t>(u * static_cast<double>(Zr));
-        draw_d = static_cast<double>(draw) / kFix;
-        const Sel sel = row_select(keys, wts, V, tok0, g, true, draw, true, area, area + kSaved, c);
-        if (sel.found) token = static_cast<int32_t>(sel.token);
-        else if (cutp.found) token = static_cast<int32_t>(cutp.token);
-        else status = Q38S_ROW_NORMALIZATION;
+    const double draw = uniform01(r.rng_before + kGamma) * Zr;
+    GLoc sel = g_locate(g, pc, pm, true, draw, true, area, c);
+    if (!sel.found || sel.idx >= r_cnt) {
+        // no prefix sum exceeds the draw (rounding): the last retained element
+        // (sampling.cc:137-144)
+        sel = cut.found ? cut
+                        : g_locate(g, pc, pm, false, static_cast<double>(r_cnt), false, area, c);
     }
     Q38S_TT(r.v, 15);
-    write_decision(a, r, token, status);
-    if (a.dist.capacity && threadIdx.x == 0) {
-        if (a.dist.n_candidates) a.dist.n_candidates[r.v] = n0;
-        if (a.dist.n_retained) a.dist.n_retained[r.v] = 0xffffffffu;
-        if (a.dist.total) a.dist.total[r.v] = static_cast<double>(Zr) / kFix;
-        if (a.dist.draw) a.dist.draw[r.v] = draw_d;
+    if (!sel.found) {
+        row_error(a, r, Q38S_ROW_NORMALIZATION);
+        return;
+    }
+    write_decision(a, r, static_cast<int32_t>(tok0 + sel.col), Q38S_ROW_OK);
+    if (a.dist.capacity) {
+        if (threadIdx.x == 0) {
+            if (a.dist.n_candidates) a.dist.n_candidates[r.v] = n0;
+            if (a.dist.n_retained) a.dist.n_retained[r.v] = r_cnt;
+            if (a.dist.total) a.dist.total[r.v] = Zr;
+            if (a.dist.draw) a.dist.draw[r.v] = draw;
+        }
+        if (a.dist.tokens || a.dist.values || a.dist.probs)
+            g_emit(a, r, g, pc, subh, n0, r_cnt, Zr, area, c);
     }
 }
 

@@ -24,8 +24,7 @@ static_assert(sizeof(q38s_sampler_state_v1) == sizeof(SamplerStateV1),
 
 namespace {
 
-[[noreturn]] void raise(int code) {
-    const std::string msg = q38s_last_error();
+[[noreturn]] void raise(int code, const std::string& msg) {
     switch (code) {
         case Q38S_INVALID_ARGUMENT: throw std::invalid_argument(msg);
         case Q38S_LOGIC_ERROR: throw std::logic_error(msg);
@@ -34,7 +33,16 @@ namespace {
 }
 
 inline void check(int code) {
-    if (code != Q38S_OK) raise(code);
+    if (code != Q38S_OK) raise(code, q38s_last_error());
+}
+
+// The message of a failed call, taken before any later call (the state
+// read-back after a commit) can replace it.
+inline std::string error_text(int code) {
+    return code != Q38S_OK ? std::string(q38s_last_error()) : std::string();
+}
+inline void check(int code, const std::string& msg) {
+    if (code != Q38S_OK) raise(code, msg);
 }
 
 SamplerDecisionV1 to_decision(const q38s_decision_v1& d) {
@@ -114,26 +122,30 @@ void TransactionalSampler::commit(const SamplerDecisionV1& decision) {
     d.rng_before = decision.rng_before;
     d.rng_after = decision.rng_after;
     const int rc = q38s_sampler_commit(engine_, &d);
+    const std::string msg = error_text(rc);
     sync_state();
-    check(rc);
+    check(rc, msg);
 }
 
 void TransactionalSampler::commit_tokens(const std::vector<std::int32_t>& tokens) {
     const int rc = q38s_sampler_commit_tokens(engine_, tokens.data(), tokens.size());
+    const std::string msg = error_text(rc);
     sync_state();
-    check(rc);
+    check(rc, msg);
 }
 
 void TransactionalSampler::commit_token(std::int32_t token) {
     const int rc = q38s_sampler_commit_tokens(engine_, &token, 1);
+    const std::string msg = error_text(rc);
     sync_state();
-    check(rc);
+    check(rc, msg);
 }
 
 void TransactionalSampler::reset() {
     const int rc = q38s_sampler_reset(engine_);
+    const std::string msg = error_text(rc);
     sync_state();
-    check(rc);
+    check(rc, msg);
 }
 
 }  // namespace q38

@@ -221,16 +221,19 @@ def check_batch(configs, logits, hists, cuda, extra=None, cap=1024):
         if dec["token"][r] != o.token:
             assert is_boundary(o, configs[r].top_p), f"row {r}: {dec['token'][r]} vs {o.token}"
             boundary += 1
-        weighted = nret[r] == -1  # kept set above 1,024: no candidate list
-        if o.n_candidates <= cap and not weighted:
-            n = o.n_candidates
-            assert ntok[r] == n, f"row {r}: {ntok[r]} candidates vs {n}"
-            if True:
-                assert (gtok[r, :n] == o.cand_tokens[:n]).all(), f"row {r}: top-k set"
-                rr = o.n_retained
-                assert nret[r] == rr
-                want = o.cand_weights[:rr] / o.total
-                np.testing.assert_allclose(gprob[r, :rr], want, rtol=PROB_RTOL, atol=0)
+        n = o.n_candidates
+        assert ntok[r] == n, f"row {r}: {ntok[r]} candidates vs {n}"
+        m = min(n, cap)
+        assert (gtok[r, :m] == o.cand_tokens[:m]).all(), f"row {r}: candidate order"
+        if nret[r] != o.n_retained:
+            # the top-p running sum sits on top_p within the tolerance
+            assert is_boundary(o, configs[r].top_p), f"row {r}: retained {nret[r]} vs {o.n_retained}"
+            continue
+        np.testing.assert_allclose(dt["total"].cpu().numpy()[r], o.total, rtol=PROB_RTOL)
+        rr = min(o.n_retained, cap)
+        want = o.cand_weights[:rr] / o.total
+        np.testing.assert_allclose(gprob[r, :rr], want, rtol=PROB_RTOL, atol=0)
+        assert (gprob[r, rr:m] == 0).all()
     return boundary
 
 
@@ -285,6 +288,54 @@ def test_general_paths(cuda):
     logits = synth.f32_to_bf16_rne(np.stack(rows))
     hists = [rng.integers(0, vocab, 2000).astype(np.int32) for _ in cfgs]
     assert check_batch(cfgs, logits, hists, cuda) == 0
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_general_path_full_distribution(dtype, cuda):
+    """top_k = 0 rows at V = 151,936 (the reference's default configuration,
+    a full sort of the vocabulary in sampling.cc:94-104): every candidate's
+    token in canonical order and every probability w_i / total within 1e-6,
+    with top_p 1.0, 0.95 and 0.5, penalties, ties and min-p."""
+    vocab = synth.VOCAB
+    rng = np.random.default_rng(1717 + (dtype == "f32"))
+    cfgs, rows = [], []
+    specs = [(0, 1.0, 0.0, 1.0), (0, 0.95, 0.0, 0.7), (0, 0.5, 0.0, 1.2), (0, 0.95, 0.0, 0.3),
+             (0, 0.9, 1e-4, 1.0), (500, 0.95, 0.0, 1.1), (0, 0.8, 0.0, 2.0), (0, 1.0, 0.0, 0.6)]
+    for r, (k, p, mp, t) in enumerate(specs):
+        x = rng.normal(0, 2.5, vocab).astype(np.float32)
+        synth.zipf_spikes(rng, x)
+        if r == 6:
+            x = np.round(x * 4) / 4  # wide tie groups
+        cfgs.append(q38s.config_v2(top_k=k, top_p=p, min_p=mp, temperature=t,
+                                   repetition_penalty=1.0 + 0.05 * (r % 3),
+                                   presence_penalty=0.2 * (r % 2), seed=5000 + r))
+        rows.append(x)
+    x = np.stack(rows)
+    logits = synth.f32_to_bf16_rne(x) if dtype == "bf16" else x
+    hists = [rng.integers(0, vocab, int(rng.integers(0, 30000))).astype(np.int32) for _ in cfgs]
+    b = check_batch(cfgs, logits, hists, cuda, cap=vocab)
+    print(f"general path {dtype}: {b} boundary cases of {len(cfgs)}")
+    assert b <= 1
+
+
+def test_general_path_edge_rows(cuda):
+    """An all-equal row (one tie group of 151,936), a row with a handful of
+    finite values among -inf, huge temperatures, and a shortened capacity."""
+    vocab = synth.VOCAB
+    rng = np.random.default_rng(1718)
+    rows, cfgs = [], []
+    x = np.full(vocab, 1.5, np.float32)
+    rows.append(x.copy()); cfgs.append(q38s.config_v2(top_k=0, top_p=0.37, seed=1))
+    rows.append(x.copy()); cfgs.append(q38s.config_v2(top_k=0, top_p=1.0, seed=2))
+    y = np.full(vocab, -np.inf, np.float32)
+    y[rng.choice(vocab, 3000, replace=False)] = rng.normal(0, 1, 3000)
+    rows.append(y); cfgs.append(q38s.config_v2(top_k=0, top_p=0.99, temperature=0.5, seed=3))
+    z = rng.normal(0, 2.5, vocab).astype(np.float32)
+    rows.append(z); cfgs.append(q38s.config_v2(top_k=0, top_p=0.999, temperature=50.0, seed=4))
+    logits = synth.f32_to_bf16_rne(np.stack(rows))
+    hists = [np.zeros(0, np.int32) for _ in cfgs]
+    assert check_batch(cfgs, logits, hists, cuda, cap=vocab) <= 1
+    assert check_batch(cfgs, logits, hists, cuda, cap=5000) <= 1
 
 
 def test_sample_commit_steps_track_oracle(cuda):
