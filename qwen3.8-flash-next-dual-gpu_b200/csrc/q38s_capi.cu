@@ -138,8 +138,10 @@ struct q38s_batch {
     uint32_t* d_counts = nullptr;
     uint32_t* d_scratch = nullptr;
     uint32_t scratch_rows = 0;
+    uint32_t* d_gen = nullptr;  // per row: deferred to the general kernel
     // speculative verification workspace
     uint32_t* d_mtp_scratch = nullptr;
+    uint32_t* d_mtp_gen = nullptr;
     int32_t* d_mtp_tokens = nullptr;
     double* d_mtp_probs = nullptr;
     uint32_t* d_mtp_nret = nullptr;
@@ -161,7 +163,9 @@ void free_batch(q38s_batch* b) {
     cudaFree(b->d_bitmap);
     cudaFree(b->d_counts);
     cudaFree(b->d_scratch);
+    cudaFree(b->d_gen);
     cudaFree(b->d_mtp_scratch);
+    cudaFree(b->d_mtp_gen);
     cudaFree(b->d_mtp_tokens);
     cudaFree(b->d_mtp_probs);
     cudaFree(b->d_mtp_nret);
@@ -222,6 +226,8 @@ int create_batch(int device, uint32_t full_vocab, uint32_t col_begin, uint32_t c
               sizeof(uint32_t) * static_cast<size_t>(columns) * rows);
     alloc(reinterpret_cast<void**>(&b->d_scratch),
           sizeof(uint32_t) * scratch_stride(columns) * rows);  // general-path keys, sums
+    alloc(reinterpret_cast<void**>(&b->d_gen), sizeof(uint32_t) * static_cast<size_t>(rows));
+    if (e == cudaSuccess) e = cudaMemset(b->d_gen, 0, sizeof(uint32_t) * rows);
     b->scratch_rows = rows;
     if (e == cudaSuccess)
         e = cudaMemcpy(b->d_params, params.data(), sizeof(RowParams) * rows,
@@ -278,6 +284,7 @@ SampleArgs base_args(const q38s_batch* b, const void* logits, uint16_t dtype,
     a.vrow_state_const = ~0u;
     a.scratch = b->d_scratch;
     a.scratch_stride = scratch_stride(b->vocab);
+    a.deferred = b->d_gen;
     return a;
 }
 
@@ -432,6 +439,8 @@ int q38s_mtp_verify(const q38s_batch* bc, uint32_t row, const void* target, cons
         if (e == cudaSuccess) e = cudaMalloc(&b->d_mtp_ncand, sizeof(uint32_t) * kMtpRows);
         if (e == cudaSuccess) e = cudaMalloc(&b->d_mtp_dec, sizeof(q38s_decision_v1) * kMtpRows);
         if (e == cudaSuccess) e = cudaMalloc(&b->d_ticket, sizeof(uint32_t));
+        if (e == cudaSuccess) e = cudaMalloc(&b->d_mtp_gen, sizeof(uint32_t) * kMtpRows);
+        if (e == cudaSuccess) e = cudaMemset(b->d_mtp_gen, 0, sizeof(uint32_t) * kMtpRows);
         if (e == cudaSuccess) e = cudaMemset(b->d_ticket, 0, sizeof(uint32_t));
         if (e != cudaSuccess) return cuda_fail(e, "speculative workspace");
     }
@@ -452,6 +461,7 @@ int q38s_mtp_verify(const q38s_batch* bc, uint32_t row, const void* target, cons
     a.dist.n_candidates = b->d_mtp_ncand;
     a.scratch = b->d_mtp_scratch;
     a.scratch_stride = scratch_stride(b->vocab);
+    a.deferred = b->d_mtp_gen;
     a.mtp = result;
     a.n_draft = n_draft;
     a.draft_tokens = draft_tokens;
@@ -841,7 +851,8 @@ constexpr uint32_t kNoAllocBitmapWords = ((kNoAllocVocab + 127) / 128) * 4;
 struct NoAllocLayout {  // byte offsets into the static array
     static constexpr size_t params = 0;
     static constexpr size_t state = params + 256;
-    static constexpr size_t bitmap = state + 256;  // cleared per call
+    static constexpr size_t gen = state + 256;     // deferred-row flags
+    static constexpr size_t bitmap = gen + 256;    // cleared per call
     static constexpr size_t scratch =  // general-path keys and sums, per row
         bitmap + sizeof(uint32_t) * static_cast<size_t>(kNoAllocBitmapWords) * kNoAllocRows;
     static constexpr size_t end =
@@ -850,6 +861,7 @@ struct NoAllocLayout {  // byte offsets into the static array
 };
 static_assert(sizeof(RowParams) * kNoAllocRows <= 256, "params slot");
 static_assert(sizeof(RowState) * kNoAllocRows <= 256, "state slot");
+static_assert(sizeof(uint32_t) * kNoAllocRows <= 256, "deferred-row slot");
 static_assert(NoAllocLayout::end % 256 == 0, "layout");
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NoAllocLayout::end];
@@ -874,6 +886,8 @@ __global__ void noalloc_stage_kernel(NoAllocRows in, uint32_t rows, uint32_t bit
         reinterpret_cast<RowParams*>(base + NoAllocLayout::params)[tid] = in.params[tid];
         reinterpret_cast<RowState*>(base + NoAllocLayout::state)[tid] = in.states[tid];
     }
+    if (tid < kNoAllocRows)  // no row deferred to the general path
+        reinterpret_cast<uint32_t*>(base + NoAllocLayout::gen)[tid] = 0u;
     uint32_t* bm = reinterpret_cast<uint32_t*>(base + NoAllocLayout::bitmap);
     const uint32_t n = rows * bitmap_words;
     for (uint32_t i = tid; i < n; i += gridDim.x * blockDim.x) bm[i] = 0u;
@@ -951,6 +965,7 @@ extern "C" int q38s_prepare_noalloc(const void* logits, uint16_t dtype, uint32_t
     a.decisions = decisions;
     a.scratch = reinterpret_cast<uint32_t*>(base + NoAllocLayout::scratch);
     a.scratch_stride = scratch_stride(vocabulary);
+    a.deferred = reinterpret_cast<uint32_t*>(base + NoAllocLayout::gen);
     a.segs = stream_segments(rows, vocabulary, device);
     const int e = launch_stream(a, stream);
     if (e != cudaSuccess) return cuda_fail(static_cast<cudaError_t>(e), "prepare_noalloc");

@@ -84,6 +84,9 @@ struct SampleArgs {
     // kGAuxWords of prefix sums and histograms
     uint32_t* scratch;
     uint64_t scratch_stride;
+    // deferred[v] != 0: virtual row v takes the general path (general
+    // kernel); zero between launches (vrows words)
+    uint32_t* deferred;
     // speculative verification, run by the last row to finish
     q38s_mtp_result* mtp;
     uint32_t n_draft;

@@ -230,7 +230,7 @@ __device__ __forceinline__ uint32_t state_row(const SampleArgs& a, uint32_t v) {
     return a.vrow_state_const != ~0u ? a.vrow_state_const : v;
 }
 
-__device__ void load_row(const SampleArgs& a, uint32_t v, Row& r) {
+__device__ __forceinline__ void load_row(const SampleArgs& a, uint32_t v, Row& r) {
     r.v = v;
     r.srow = state_row(a, v);
     r.p = a.params[r.srow];
@@ -703,7 +703,8 @@ __device__ void epilogue(const uint64_t* sorted, uint32_t n, const RowParams& p,
 }
 
 // ---------------------------------------------------------------- outputs
-__device__ void write_decision(const SampleArgs& a, const Row& r, int32_t token, int32_t status) {
+__device__ __forceinline__ void write_decision(const SampleArgs& a, const Row& r, int32_t token,
+                                               int32_t status) {
     if (threadIdx.x != 0) return;
     q38s_decision_v1 d;
     d.token = status == Q38S_ROW_OK ? token : -1;
@@ -739,7 +740,8 @@ __device__ void write_decision(const SampleArgs& a, const Row& r, int32_t token,
     }
 }
 
-__device__ void write_distribution(const SampleArgs& a, const Row& r, const uint64_t* sorted,
+__device__ __forceinline__ void write_distribution(const SampleArgs& a, const Row& r,
+                                                   const uint64_t* sorted,
                                    const double* w, Ctl& c) {
     if (a.dist.capacity == 0) return;
     const uint32_t cap = a.dist.capacity;
@@ -760,7 +762,7 @@ __device__ void write_distribution(const SampleArgs& a, const Row& r, const uint
     }
 }
 
-__device__ void row_error(const SampleArgs& a, const Row& r, int32_t status) {
+__device__ __forceinline__ void row_error(const SampleArgs& a, const Row& r, int32_t status) {
     if (a.mode == kModeShardTopK) {
         for (uint32_t i = threadIdx.x; i < a.k_out; i += kCons) {
             q38s_candidate cd;
@@ -778,7 +780,8 @@ __device__ void row_error(const SampleArgs& a, const Row& r, int32_t status) {
 }
 
 // Final outputs of a row from its sorted candidate list.
-__device__ void row_output(const SampleArgs& a, const Row& r, const uint64_t* sorted,
+__device__ __forceinline__ void row_output(const SampleArgs& a, const Row& r,
+                                           const uint64_t* sorted,
                            uint32_t keep, double* w, double* S, double* q, Ctl& c) {
     if (a.mode == kModeShardTopK) {
         for (uint32_t i = threadIdx.x; i < a.k_out; i += kCons) {
@@ -813,7 +816,7 @@ __device__ void row_output(const SampleArgs& a, const Row& r, const uint64_t* so
 // draft or support entry); the first draft that is not accepted ends the
 // walk; the sequential sums of the residual draw run in one thread, in the
 // order written here.  Other CTAs wrote the arrays read here: L2 loads.
-__device__ void mtp_finish(const SampleArgs& a, unsigned char* area, Ctl& c) {
+__device__ __forceinline__ void mtp_finish(const SampleArgs& a, unsigned char* area, Ctl& c) {
     const uint32_t n = a.n_draft;
     const uint32_t cap = a.dist.capacity;
     const uint32_t tid = threadIdx.x;
@@ -987,7 +990,7 @@ __device__ void mtp_finish(const SampleArgs& a, unsigned char* area, Ctl& c) {
 }
 
 // A virtual row is complete: the last one runs the speculative verification.
-__device__ void row_done(const SampleArgs& a, unsigned char* area, Ctl& c) {
+__device__ __forceinline__ void row_done(const SampleArgs& a, unsigned char* area, Ctl& c) {
     if (!a.mtp) return;
     cbar();
     // one GPU-scope acquire-release ticket: it publishes this row's outputs
@@ -1044,6 +1047,7 @@ static_assert(kGB * 12 <= kArea && kGL * 16 + (kGB + 1) * 4 <= kArea, "general-p
 
 struct GRow {
     const uint32_t* keys;  // exact key per column (padded to whole 16-byte groups)
+    uint4* stage;          // the passes' cp.async slots (kStageBytes of shared memory)
     uint32_t V, tok0;
     float M;               // the row maximum
     uint32_t minp_key;     // smallest key whose weight reaches min_p (0: no min-p)
@@ -1051,13 +1055,13 @@ struct GRow {
     uint32_t cut_key, cut_col;
 };
 
-__device__ __forceinline__ bool g_in(const GRow& g, uint32_t key, uint32_t col) {
+__device__ __forceinline__ bool g_in(const GRow g, uint32_t key, uint32_t col) {
     if (key < g.minp_key) return false;
     if (!g.has_cut) return true;
     return key > g.cut_key || (key == g.cut_key && col <= g.cut_col);
 }
 // Distance d = fl(M - v) (the negated fl(v - M) of the reference) and its bin.
-__device__ __forceinline__ uint32_t g_bin(const GRow& g, uint32_t key, float& d) {
+__device__ __forceinline__ uint32_t g_bin(const GRow g, uint32_t key, float& d) {
     d = __fsub_rn(g.M, key_float(key));
     const float s = __fmul_rn(d, 32.0f);
     return s < static_cast<float>(kGB - 1) ? static_cast<uint32_t>(s) : kGB - 1;
@@ -1077,7 +1081,7 @@ __device__ __forceinline__ unsigned long long g_tw(float d, uint32_t b) {
     return __double2ull_rn(t * kGUnit);
 }
 // The reference's weight of a key, exp((double)fl(v - M)) (sampling.cc:112).
-__device__ __forceinline__ double g_weight(const GRow& g, uint32_t key) {
+__device__ __forceinline__ double g_weight(const GRow g, uint32_t key) {
     return exp(static_cast<double>(__fsub_rn(key_float(key), g.M)));
 }
 __device__ __forceinline__ double g_bin_scale(uint32_t b) {
@@ -1085,7 +1089,7 @@ __device__ __forceinline__ double g_bin_scale(uint32_t b) {
 }
 
 // Exclusive prefix sum of doubles over the consumers in thread order.
-__device__ double cscan_excl_f64(double v, double* total, Ctl& c) {
+__device__ __forceinline__ double cscan_excl_f64(double v, double* total, Ctl& c) {
     const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     double inc = v;
     for (int o = 1; o < 32; o <<= 1) {
@@ -1107,85 +1111,122 @@ __device__ double cscan_excl_f64(double v, double* total, Ctl& c) {
     return before + excl;
 }
 
-// Visits every column j < V with its key, eight 16-byte groups of keys per
-// thread in flight; f(col, key, valid) runs a warp-uniform number of times.
-template <typename F>
-__device__ __forceinline__ void g_for_keys(const GRow& g, F&& f) {
-    constexpr int kIn = 8;
-    const uint32_t nq = (g.V + 3) / 4;
-    const uint4* kq = reinterpret_cast<const uint4*>(g.keys);
-    for (uint32_t base = 0; base < nq; base += kIn * kCons) {
-        uint4 kv[kIn];
-#pragma unroll
-        for (int i = 0; i < kIn; ++i) {
-            const uint32_t q = base + i * kCons + threadIdx.x;
-            kv[i] = q < nq ? __ldcg(kq + q) : make_uint4(0u, 0u, 0u, 0u);
-        }
-#pragma unroll
-        for (int i = 0; i < kIn; ++i) {
-            const uint32_t c0 = (base + i * kCons + threadIdx.x) * 4;
-            f(c0, kv[i].x, c0 < g.V);
-            f(c0 + 1, kv[i].y, c0 + 1 < g.V);
-            f(c0 + 2, kv[i].z, c0 + 2 < g.V);
-            f(c0 + 3, kv[i].w, c0 + 3 < g.V);
-        }
-    }
+// Pipelined passes of the general kernel: every thread streams its own
+// 16-byte groups (group r * kCons + tid in round r) through kStages cp.async
+// slots of shared memory, kStages - 1 rounds ahead of their use, so 64 KB per
+// CTA are in flight without holding registers.  Each thread reads only the
+// slots it filled; a slot is refilled after its value was consumed.
+constexpr uint32_t kStages = 16;
+constexpr uint32_t kStageBytes = kStages * kCons * 16;
+static_assert(kStageBytes <= kRing * kSlot, "general-path stages in the ring");
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)),
+                 "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// P1: the exact key of every column into g.keys (16-byte stores), eight
-// 16-byte groups of logits per thread in flight.  Returns the largest key.
+// f(group, 16 bytes, valid) over the nbytes at src (16-byte aligned); a ragged
+// last group is zero-filled past its end.  Warp-uniform round count.
+template <typename F>
+__device__ __forceinline__ void g_pass16(const unsigned char* src, uint64_t nbytes, uint4* stage,
+                                         F&& f) {
+    const uint32_t n16 = static_cast<uint32_t>((nbytes + 15) / 16);
+    const uint32_t rounds = (n16 + kCons - 1) / kCons;
+    auto issue = [&](uint32_t r) {
+        const uint32_t gi = r * kCons + threadIdx.x;
+        if (r < rounds && gi < n16) {
+            const uint64_t off = static_cast<uint64_t>(gi) * 16;
+            const uint32_t bytes = nbytes - off >= 16 ? 16u : static_cast<uint32_t>(nbytes - off);
+            cp_async16(&stage[(r % kStages) * kCons + threadIdx.x], src + off, bytes);
+        }
+        cp_async_commit();  // one group per round, so the wait counts stay aligned
+    };
+    for (uint32_t r = 0; r + 1 < kStages; ++r) issue(r);
+    for (uint32_t r = 0; r < rounds; ++r) {
+        issue(r + kStages - 1);
+        cp_async_wait<kStages - 1>();
+        const uint32_t gi = r * kCons + threadIdx.x;
+        const uint4 v = gi < n16 ? stage[(r % kStages) * kCons + threadIdx.x]
+                                 : make_uint4(0u, 0u, 0u, 0u);
+        f(gi, v, gi < n16);
+    }
+    cp_async_wait<0>();
+}
+
+// Visits every column j < V with its key; f(col, key, valid) runs a
+// warp-uniform number of times.
+template <typename F>
+__device__ __forceinline__ void g_for_keys(const GRow g, F&& f) {
+    g_pass16(reinterpret_cast<const unsigned char*>(g.keys), static_cast<uint64_t>(g.V) * 4, g.stage,
+             [&](uint32_t gi, const uint4& kv, bool) {
+                 const uint32_t c0 = gi * 4;
+                 f(c0, kv.x, c0 < g.V);
+                 f(c0 + 1, kv.y, c0 + 1 < g.V);
+                 f(c0 + 2, kv.z, c0 + 2 < g.V);
+                 f(c0 + 3, kv.w, c0 + 3 < g.V);
+             });
+}
+
+// P1: the exact key (sampling.cc:76-92) of every column into keys (16-byte
+// stores); the logits arrive through the pipelined pass when rows are
+// 16-byte aligned.  Returns the largest key.
 template <int DT>
-__device__ uint32_t g_keys(const SampleArgs& a, const Row& r, const unsigned char* row,
-                           const uint32_t* pbm, uint32_t* keys, uint32_t V, Ctl& c) {
+__device__ __forceinline__ uint32_t g_keys(const SampleArgs& a, const Row& r, const unsigned char* row,
+                                           const uint32_t* pbm, uint32_t* keys, uint32_t V,
+                                           uint4* stage, Ctl& c) {
     constexpr uint32_t es = DT == Q38S_DTYPE_BF16 ? 2u : 4u;
     constexpr uint32_t pv = 16u / es;
-    constexpr int kIn = 8;
-    const uint32_t nvec = (V + pv - 1) / pv;
     uint32_t kmax = 0;
-    for (uint32_t base = 0; base < nvec; base += kIn * kCons) {
-        uint4 w[kIn];
+    auto group = [&](uint32_t q, const uint4& w) {
+        const uint32_t col0 = q * pv;
+        uint32_t pw = 0;  // penalised bits of the 32-column word holding the group
+        if (r.pen) pw = pbm ? pbm[col0 >> 5] : r.gbm[col0 >> 5];
+        uint32_t k[pv];
 #pragma unroll
-        for (int i = 0; i < kIn; ++i) {
-            const uint32_t q = base + i * kCons + threadIdx.x;
-            w[i] = q < nvec ? load_vec<DT>(a, row, q * pv, min(pv, V - q * pv))
-                            : make_uint4(0u, 0u, 0u, 0u);
-        }
-#pragma unroll
-        for (int i = 0; i < kIn; ++i) {
-            const uint32_t q = base + i * kCons + threadIdx.x;
-            if (q >= nvec) continue;
-            const uint32_t col0 = q * pv;
-            uint32_t pw = 0;  // penalised bits of the 32-column word holding the vector
-            if (r.pen) pw = pbm ? pbm[col0 >> 5] : r.gbm[col0 >> 5];
-            uint32_t k[pv];
-#pragma unroll
-            for (uint32_t e = 0; e < pv; ++e) {
-                const uint32_t col = col0 + e;
-                bool pen = false;
-                uint64_t count = 1;
-                if (r.pen && col < V) {
-                    const uint64_t ex = (!pbm && r.n_extra) ? extra_count(r, a.col_begin + col) : 0u;
-                    pen = ((pw >> (col & 31)) & 1u) || ex != 0;
-                    if (pen && r.freq)
-                        count = (r.counts_row ? r.counts_row[col] : 0u) +
-                                (pbm ? extra_count(r, a.col_begin + col) : ex);
-                }
-                k[e] = col < V ? float_key(transform(vec_elem<DT>(w[i], static_cast<int>(e)), pen,
-                                                     count, r.p))
-                               : 0u;
-                kmax = max(kmax, k[e]);
+        for (uint32_t e = 0; e < pv; ++e) {
+            const uint32_t col = col0 + e;
+            bool pen = false;
+            uint64_t count = 1;
+            if (r.pen && col < V) {
+                const uint64_t ex = (!pbm && r.n_extra) ? extra_count(r, a.col_begin + col) : 0u;
+                pen = ((pw >> (col & 31)) & 1u) || ex != 0;
+                if (pen && r.freq)
+                    count = (r.counts_row ? r.counts_row[col] : 0u) +
+                            (pbm ? extra_count(r, a.col_begin + col) : ex);
             }
-            if (col0 + pv <= V) {
-                uint4* dst = reinterpret_cast<uint4*>(keys + col0);
-                dst[0] = make_uint4(k[0], k[1], k[2], k[3]);
-                if (pv == 8) dst[1] = make_uint4(k[pv == 8 ? 4 : 0], k[pv == 8 ? 5 : 0],
-                                                 k[pv == 8 ? 6 : 0], k[pv == 8 ? 7 : 0]);
-            } else {
-#pragma unroll
-                for (uint32_t e = 0; e < pv; ++e)
-                    if (col0 + e < V) keys[col0 + e] = k[e];
-            }
+            k[e] = col < V ? float_key(transform(vec_elem<DT>(w, static_cast<int>(e)), pen, count,
+                                                 r.p))
+                           : 0u;
+            kmax = max(kmax, k[e]);
         }
+        if (col0 + pv <= V) {
+            uint4* dst = reinterpret_cast<uint4*>(keys + col0);
+            dst[0] = make_uint4(k[0], k[1], k[2], k[3]);
+            if (pv == 8)
+                dst[1] = make_uint4(k[pv == 8 ? 4 : 0], k[pv == 8 ? 5 : 0], k[pv == 8 ? 6 : 0],
+                                    k[pv == 8 ? 7 : 0]);
+        } else {
+#pragma unroll
+            for (uint32_t e = 0; e < pv; ++e)
+                if (col0 + e < V) keys[col0 + e] = k[e];
+        }
+    };
+    if (a.use_tma) {
+        g_pass16(row, static_cast<uint64_t>(V) * es, stage, [&](uint32_t q, const uint4& w, bool valid) {
+            if (valid) group(q, w);
+        });
+    } else {
+        const uint32_t nvec = (V + pv - 1) / pv;
+        for (uint32_t q = threadIdx.x; q < nvec; q += kCons)
+            group(q, load_vec<DT>(a, row, q * pv, min(pv, V - q * pv)));
     }
     return cmax_u32(kmax, c);  // its barriers also publish keys[] to the CTA
 }
@@ -1193,7 +1234,7 @@ __device__ uint32_t g_keys(const SampleArgs& a, const Row& r, const unsigned cha
 // P2: histogram of K0 over the distance bins, then each bin's exclusive
 // prefix count (pc) and, when weighted, mass (pm); pc[kGB] / pm[kGB] hold
 // the totals.  Returns |K0|; *Z gets its mass.
-__device__ uint32_t g_level1(const GRow& g, bool weighted, unsigned char* area, uint32_t* pc,
+__device__ __forceinline__ uint32_t g_level1(const GRow g, bool weighted, unsigned char* area, uint32_t* pc,
                              double* pm, double* Z, Ctl& c) {
     uint32_t* hc = reinterpret_cast<uint32_t*>(area);
     unsigned long long* hm = reinterpret_cast<unsigned long long*>(area + kGB * 4);
@@ -1259,7 +1300,7 @@ struct GSpan {          // the K0 members with distance bin b1 and key in [lo, h
     uint32_t n;          // K0 elements in the span
 };
 
-__device__ __forceinline__ bool g_member(const GRow& g, const GSpan& s, uint32_t key,
+__device__ __forceinline__ bool g_member(const GRow g, const GSpan s, uint32_t key,
                                          uint32_t col) {
     if (key < s.lo || key > s.hi || !g_in(g, key, col)) return false;
     float d;
@@ -1267,7 +1308,7 @@ __device__ __forceinline__ bool g_member(const GRow& g, const GSpan& s, uint32_t
 }
 
 // Smallest and largest key of the span's members.
-__device__ void g_minmax(const GRow& g, GSpan& s, Ctl& c) {
+__device__ __forceinline__ void g_minmax(const GRow g, GSpan& s, Ctl& c) {
     uint32_t lo = 0xffffffffu, hi = 0;
     g_for_keys(g, [&](uint32_t col, uint32_t key, bool valid) {
         if (valid && g_member(g, s, key, col)) {
@@ -1281,7 +1322,7 @@ __device__ void g_minmax(const GRow& g, GSpan& s, Ctl& c) {
 
 // The span's members as rank keys, sorted descending into `sorted`
 // (gathered in `buf`); returns their number (at most kGL).
-__device__ uint32_t g_gather_sorted(const GRow& g, const GSpan& s, uint32_t blo, uint32_t bhi,
+__device__ __forceinline__ uint32_t g_gather_sorted(const GRow g, const GSpan s, uint32_t blo, uint32_t bhi,
                                     uint64_t* buf, uint64_t* sorted, Ctl& c) {
     cbar();
     if (threadIdx.x == 0) c.bc_u32[2] = 0;
@@ -1303,7 +1344,7 @@ __device__ uint32_t g_gather_sorted(const GRow& g, const GSpan& s, uint32_t blo,
 
 // The located element inside a span of at most kGL members: exact weights
 // summed in canonical order from the mass above the span.
-__device__ GLoc g_final(const GRow& g, const GSpan& s, bool mass, double tau, bool strict,
+__device__ __forceinline__ GLoc g_final(const GRow g, const GSpan s, bool mass, double tau, bool strict,
                         unsigned char* area, Ctl& c) {
     uint64_t* buf = reinterpret_cast<uint64_t*>(area);
     uint64_t* lk = reinterpret_cast<uint64_t*>(area + kGL * 8);
@@ -1361,7 +1402,7 @@ __device__ GLoc g_final(const GRow& g, const GSpan& s, bool mass, double tau, bo
 
 // The j-th smallest column among the K0 members holding `key`: a radix over
 // the column bits, 11 then 9 bits (columns < 2^20).
-__device__ uint32_t g_tie_col(const GRow& g, uint32_t key, uint32_t j, unsigned char* area,
+__device__ __forceinline__ uint32_t g_tie_col(const GRow g, uint32_t key, uint32_t j, unsigned char* area,
                               Ctl& c) {
     uint32_t* h = reinterpret_cast<uint32_t*>(area);
     uint32_t prefix = 0, need = j;
@@ -1393,7 +1434,7 @@ __device__ uint32_t g_tie_col(const GRow& g, uint32_t key, uint32_t j, unsigned 
 }
 
 // The located element in a tie group (a span holding one key).
-__device__ GLoc g_tie(const GRow& g, const GSpan& s, bool mass, double tau, bool strict,
+__device__ __forceinline__ GLoc g_tie(const GRow g, const GSpan s, bool mass, double tau, bool strict,
                       unsigned char* area, Ctl& c) {
     const uint32_t key = s.lo;
     const double w = g_weight(g, key);
@@ -1416,7 +1457,7 @@ __device__ GLoc g_tie(const GRow& g, const GSpan& s, bool mass, double tau, bool
 
 // First K0 element at which the running count (mass false: tau an integer
 // count) or mass reaches tau (>= tau, or > tau when strict).
-__device__ GLoc g_locate(const GRow& g, const uint32_t* pc, const double* pm, bool mass,
+__device__ __forceinline__ GLoc g_locate(const GRow g, const uint32_t* pc, const double* pm, bool mass,
                          double tau, bool strict, unsigned char* area, Ctl& c) {
     constexpr uint32_t kPer = kGB / kCons;
     // the bin: first b whose running total through it reaches tau
@@ -1547,65 +1588,62 @@ __device__ GLoc g_locate(const GRow& g, const uint32_t* pc, const double* pm, bo
 // ---- distribution output of a general row: K0's first n_emit members in
 // canonical order with their values, and w_i / Z_r for the first r_cnt.
 struct GOut {
+    int32_t* tokens;  // the distribution arrays (any may be null)
+    float* values;
+    double* probs;
     size_t base;      // row offset in the distribution arrays
     uint32_t n_emit;
     uint32_t r_cnt;
     double Zr;
 };
 
-__device__ void g_write_list(const SampleArgs& a, const GRow& g, const GOut& o, const uint64_t* lk,
+__device__ __forceinline__ void g_write_list(const GRow g, const GOut o, const uint64_t* lk,
                              uint32_t n, uint32_t pos) {
     for (uint32_t i = threadIdx.x; i < n; i += kCons) {
         const uint32_t p = pos + i;
         if (p >= o.n_emit) break;
         const uint32_t key = static_cast<uint32_t>(lk[i] >> 32);
-        if (a.dist.tokens) a.dist.tokens[o.base + p] = static_cast<int32_t>(rank_token(lk[i]));
-        if (a.dist.values) a.dist.values[o.base + p] = key_float(key);
-        if (a.dist.probs) a.dist.probs[o.base + p] = p < o.r_cnt ? g_weight(g, key) / o.Zr : 0.0;
+        if (o.tokens) o.tokens[o.base + p] = static_cast<int32_t>(rank_token(lk[i]));
+        if (o.values) o.values[o.base + p] = key_float(key);
+        if (o.probs) o.probs[o.base + p] = p < o.r_cnt ? g_weight(g, key) / o.Zr : 0.0;
     }
     cbar();
 }
 
-// The K0 members holding `key` in column order (a tie group), at pos.
-__device__ void g_write_tie(const SampleArgs& a, const GRow& g, const GOut& o, uint32_t key,
-                            uint32_t pos, Ctl& c) {
+// The K0 members holding `key` in column order (a tie group), at pos: each
+// round of the pass covers 4 * kCons consecutive columns in thread order.
+__device__ __forceinline__ void g_write_tie(const GRow g, const GOut o, uint32_t key, uint32_t pos,
+                                            Ctl& c) {
     const float val = key_float(key);
     const double w = g_weight(g, key);
-    const uint4* kq = reinterpret_cast<const uint4*>(g.keys);
-    for (uint32_t c0 = 0; c0 < g.V && pos < o.n_emit; c0 += 16 * kCons) {
-        const uint32_t my0 = c0 + threadIdx.x * 16;  // 16 consecutive columns per thread
-        uint32_t flags = 0;
+    g_pass16(reinterpret_cast<const unsigned char*>(g.keys), static_cast<uint64_t>(g.V) * 4, g.stage,
+             [&](uint32_t gi, const uint4& kv, bool) {
+                 const uint32_t kk[4] = {kv.x, kv.y, kv.z, kv.w};
+                 uint32_t flags = 0;
 #pragma unroll
-        for (uint32_t q = 0; q < 4; ++q) {
-            const uint32_t cq = my0 + 4 * q;
-            if (cq < g.V) {
-                const uint4 kv = __ldcg(kq + cq / 4);
-                const uint32_t kk[4] = {kv.x, kv.y, kv.z, kv.w};
-#pragma unroll
-                for (uint32_t e = 0; e < 4; ++e)
-                    if (cq + e < g.V && kk[e] == key && g_in(g, key, cq + e))
-                        flags |= 1u << (4 * q + e);
-            }
-        }
-        uint32_t tot;
-        uint32_t off = cscan_excl(__popc(flags), &tot, c);
-        while (flags) {
-            const uint32_t e = __ffs(flags) - 1;
-            flags &= flags - 1;
-            const uint32_t p = pos + off++;
-            if (p < o.n_emit) {
-                if (a.dist.tokens) a.dist.tokens[o.base + p] = static_cast<int32_t>(g.tok0 + my0 + e);
-                if (a.dist.values) a.dist.values[o.base + p] = val;
-                if (a.dist.probs) a.dist.probs[o.base + p] = p < o.r_cnt ? w / o.Zr : 0.0;
-            }
-        }
-        pos += tot;
-    }
+                 for (uint32_t e = 0; e < 4; ++e) {
+                     const uint32_t col = gi * 4 + e;
+                     if (col < g.V && kk[e] == key && g_in(g, key, col)) flags |= 1u << e;
+                 }
+                 uint32_t tot;
+                 uint32_t off = cscan_excl(__popc(flags), &tot, c);
+                 while (flags) {
+                     const uint32_t e = __ffs(flags) - 1;
+                     flags &= flags - 1;
+                     const uint32_t p = pos + off++;
+                     if (p < o.n_emit) {
+                         if (o.tokens) o.tokens[o.base + p] = static_cast<int32_t>(g.tok0 + gi * 4 + e);
+                         if (o.values) o.values[o.base + p] = val;
+                         if (o.probs) o.probs[o.base + p] = p < o.r_cnt ? w / o.Zr : 0.0;
+                     }
+                 }
+                 pos += tot;
+             });
     cbar();
 }
 
 // Counts of the key sub-bins of a span (highest keys first) into h.
-__device__ void g_subcount(const GRow& g, const GSpan& s, int sh, uint32_t top, uint32_t* h) {
+__device__ __forceinline__ void g_subcount(const GRow g, const GSpan s, int sh, uint32_t top, uint32_t* h) {
     cbar();
     for (uint32_t i = threadIdx.x; i < kGB; i += kCons) h[i] = 0;
     cbar();
@@ -1619,7 +1657,7 @@ __device__ void g_subcount(const GRow& g, const GSpan& s, int sh, uint32_t top, 
 // (sub-bin counts of the open levels in scratch, the current one in shared
 // memory), groups of consecutive small sub-bins gathered and sorted, single
 // keys written as tie groups.
-__device__ void g_emit_big(const SampleArgs& a, const GRow& g, const GOut& o, GSpan root,
+__device__ __forceinline__ void g_emit_big(const GRow g, const GOut o, GSpan root,
                            uint32_t pos, uint32_t* subh, unsigned char* area, Ctl& c) {
     uint64_t* buf = reinterpret_cast<uint64_t*>(area);
     uint64_t* lk = reinterpret_cast<uint64_t*>(area + kGL * 8);
@@ -1647,7 +1685,7 @@ __device__ void g_emit_big(const SampleArgs& a, const GRow& g, const GOut& o, GS
         cbar();
     };
     if (root.lo == root.hi) {
-        g_write_tie(a, g, o, root.lo, pos, c);
+        g_write_tie(g, o, root.lo, pos, c);
         return;
     }
     open(0, root.lo, root.hi, pos);
@@ -1664,7 +1702,7 @@ __device__ void g_emit_big(const SampleArgs& a, const GRow& g, const GOut& o, GS
             const uint32_t hi2 = f.sh ? min(f.hi, lo2 + ((1u << f.sh) - 1u)) : lo2;
             if (cnt > kGL) {
                 if (lo2 == hi2 || d + 1 >= static_cast<int>(kEmitDepth)) {
-                    g_write_tie(a, g, o, lo2, f.pos, c);
+                    g_write_tie(g, o, lo2, f.pos, c);
                     f.pos += cnt;
                     ++f.sb;
                     continue;
@@ -1684,7 +1722,7 @@ __device__ void g_emit_big(const SampleArgs& a, const GRow& g, const GOut& o, GS
             s.lo = f.lo + ((f.top - (e - 1)) << f.sh);
             s.hi = hi2;
             const uint32_t n = g_gather_sorted(g, s, root.b1, root.b1, buf, lk, c);
-            g_write_list(a, g, o, lk, n, f.pos);
+            g_write_list(g, o, lk, n, f.pos);
             f.pos += n;
             f.sb = e;
         }
@@ -1698,17 +1736,11 @@ __device__ void g_emit_big(const SampleArgs& a, const GRow& g, const GOut& o, GS
     }
 }
 
-__device__ void g_emit(const SampleArgs& a, const Row& r, const GRow& g, const uint32_t* pc,
-                       uint32_t* subh, uint32_t n0, uint32_t r_cnt, double Zr, unsigned char* area,
-                       Ctl& c) {
+__device__ __forceinline__ void g_emit(const GRow g, const GOut o, const uint32_t* pc, uint32_t* subh,
+                       unsigned char* area, Ctl& c) {
     uint64_t* buf = reinterpret_cast<uint64_t*>(area);
     uint64_t* lk = reinterpret_cast<uint64_t*>(area + kGL * 8);
     uint32_t* bcnt = reinterpret_cast<uint32_t*>(area + kGL * 16);  // level-1 counts
-    GOut o;
-    o.base = static_cast<size_t>(r.v) * a.dist.capacity;
-    o.n_emit = min(n0, a.dist.capacity);
-    o.r_cnt = r_cnt;
-    o.Zr = Zr;
     cbar();
     for (uint32_t b = threadIdx.x; b < kGB; b += kCons) bcnt[b] = __ldcg(&pc[b + 1]) - __ldcg(&pc[b]);
     cbar();
@@ -1728,7 +1760,7 @@ __device__ void g_emit(const SampleArgs& a, const Row& r, const GRow& g, const u
         s.n = cnt;
         if (cnt > kGL) {
             g_minmax(g, s, c);
-            g_emit_big(a, g, o, s, pos, subh, area, c);
+            g_emit_big(g, o, s, pos, subh, area, c);
             // the level-1 counts live beside the sub-bin counts: reload them
             cbar();
             for (uint32_t i = threadIdx.x; i < kGB; i += kCons)
@@ -1741,16 +1773,15 @@ __device__ void g_emit(const SampleArgs& a, const Row& r, const GRow& g, const u
         uint32_t e = b + 1, tot = cnt;
         while (e < kGB && tot + bcnt[e] <= kGL) tot += bcnt[e++];
         const uint32_t n = g_gather_sorted(g, s, b, e - 1, buf, lk, c);
-        g_write_list(a, g, o, lk, n, pos);
+        g_write_list(g, o, lk, n, pos);
         pos += n;
         b = e;
     }
 }
 
-// Out of line: the general path's register needs stay out of the stream loop.
 template <int DT>
-__device__ __noinline__ void general_row(const SampleArgs& a, const Row& r, unsigned char* area,
-                                         Ctl& c) {
+__device__ __forceinline__ void general_row(const SampleArgs& a, const Row& r, unsigned char* area,
+                                            uint4* stage, Ctl& c) {
     const uint32_t V = a.vocab;
     const uint32_t tok0 = a.col_begin;
     uint32_t* keys = a.scratch + static_cast<size_t>(r.v) * a.scratch_stride;
@@ -1777,9 +1808,10 @@ __device__ __noinline__ void general_row(const SampleArgs& a, const Row& r, unsi
     }
     GRow g;
     g.keys = keys;
+    g.stage = stage;
     g.V = V;
     g.tok0 = tok0;
-    const uint32_t M_key = g_keys<DT>(a, r, row, pbm, keys, V, c);
+    const uint32_t M_key = g_keys<DT>(a, r, row, pbm, keys, V, g.stage, c);
     Q38S_TT(r.v, 6);
     g.M = key_float(M_key);
     g.minp_key = 0;
@@ -1882,26 +1914,76 @@ __device__ __noinline__ void general_row(const SampleArgs& a, const Row& r, unsi
             if (a.dist.total) a.dist.total[r.v] = Zr;
             if (a.dist.draw) a.dist.draw[r.v] = draw;
         }
-        if (a.dist.tokens || a.dist.values || a.dist.probs)
-            g_emit(a, r, g, pc, subh, n0, r_cnt, Zr, area, c);
+        if (a.dist.tokens || a.dist.values || a.dist.probs) {
+            GOut o;
+            o.tokens = a.dist.tokens;
+            o.values = a.dist.values;
+            o.probs = a.dist.probs;
+            o.base = static_cast<size_t>(r.v) * a.dist.capacity;
+            o.n_emit = min(n0, a.dist.capacity);
+            o.r_cnt = r_cnt;
+            o.Zr = Zr;
+            g_emit(g, o, pc, subh, area, c);
+        }
     }
 }
 
 // Completes a row once its candidate list (or failure) is known.
 template <int DT>
-__device__ void finish_row(const SampleArgs& a, const Row& r, uint32_t flags,
-                           const uint64_t* sorted, uint32_t keep, unsigned char* area, Ctl& c) {
+__device__ __forceinline__ void finish_row(const SampleArgs& a, const Row& r, uint32_t flags,
+                                           const uint64_t* sorted, uint32_t keep,
+                                           unsigned char* area, Ctl& c) {
     if (flags & kFTimeout) {
         row_error(a, r, Q38S_ROW_TIMEOUT);
     } else if (flags & kFInf) {
         row_error(a, r, Q38S_ROW_NO_FINITE);
     } else if (flags & kFOverflow) {
-        general_row<DT>(a, r, area, c);
+        // the general path runs in general_kernel, launched behind this one
+        if (threadIdx.x == 0) a.deferred[r.v] = 1u;
+        return;
     } else {
         double* w = reinterpret_cast<double*>(area);  // over the dead candidate buffer
         row_output(a, r, sorted, keep, w, w + kFinal, w + 2 * kFinal, c);
     }
     row_done(a, area, c);
+}
+
+// ------------------------------------------------------------ general kernel
+// The rows the stream kernel deferred (deferred[v] != 0), one CTA per row at
+// a time; row v belongs to CTA v % gridDim.x.  Launched right behind the
+// stream kernel as its programmatic dependent: it may be scheduled early and
+// waits (griddepcontrol.wait) until the stream kernel has completed.  Each
+// CTA reads its rows' flags in one load per thread and clears the flags it
+// takes, so the flags are zero between launches; with no deferred row it
+// returns at once.  The stream kernel stays free of the general path's code.
+template <int DT>
+__global__ void __launch_bounds__(kCons, 1) general_kernel(const SampleArgs a) {
+    extern __shared__ __align__(1024) unsigned char gsm[];
+    __shared__ Ctl c;
+    __shared__ Row rs;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    unsigned char* area = gsm;
+    uint4* stage = reinterpret_cast<uint4*>(gsm + kArea);
+    for (uint32_t base = blockIdx.x; base < a.vrows; base += gridDim.x * kCons) {
+        const uint32_t v = base + threadIdx.x * gridDim.x;
+        const uint32_t mine = v < a.vrows && a.deferred[v] != 0 ? 1u : 0u;
+        uint32_t n;
+        const uint32_t pos = cscan_excl(mine, &n, c);  // the flagged rows, in order
+        if (mine) c.tkey[pos] = v;
+        cbar();
+        for (uint32_t i = 0; i < n; ++i) {
+            const uint32_t vr = c.tkey[i];
+            cbar();
+            if (threadIdx.x == 0) {
+                a.deferred[vr] = 0;
+                load_row(a, vr, rs);
+            }
+            cbar();
+            general_row<DT>(a, rs, area, stage, c);
+            row_done(a, area, c);
+            cbar();
+        }
+    }
 }
 
 // ------------------------------------------------------------ the kernel
@@ -1914,8 +1996,11 @@ __device__ __forceinline__ void chunk_range(uint32_t vocab, uint32_t S, uint32_t
     hi = min(b1 * 128u, vocab);
 }
 
-__device__ bool wait_full(Ctl& c, uint32_t slot, uint32_t phase, long long limit) {
+__device__ bool wait_full(const SampleArgs& a, Ctl& c, uint32_t slot, uint32_t phase) {
     if (mbar_try_wait(&c.full[slot], phase)) return true;
+    // the limit (a test may shorten the first CTA's) is read only when waiting
+    const long long limit =
+        (a.test_withhold && blockIdx.x == 0) ? a.test_wait_cycles : kWaitLimitCycles;
     const long long start = clock64();
     while (!mbar_try_wait(&c.full[slot], phase)) {
         if (*reinterpret_cast<volatile uint32_t*>(&c.abort_flag)) return false;
@@ -1983,6 +2068,10 @@ template <int DT>
 __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
     extern __shared__ __align__(1024) unsigned char dsm[];
     __shared__ Ctl c;
+    __shared__ Row rs;
+    // the general kernel behind this one may be scheduled now; it waits for
+    // this grid's completion before it reads anything this grid writes
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     constexpr uint32_t es = DT == Q38S_DTYPE_BF16 ? 2u : 4u;
     constexpr uint32_t pv = 16u / es;  // elements per 16-byte vector
     constexpr uint32_t TC = kTileBytes / es;
@@ -2034,8 +2123,6 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
     const uint32_t n_units = a.vrows * S;
     uint32_t g = 0;     // tiles passed (the producer's order)
     uint32_t xrow = 0;  // multi-segment rows passed (the cluster barriers' parity)
-    const long long tile_wait =
-        (a.test_withhold && blockIdx.x == 0) ? a.test_wait_cycles : kWaitLimitCycles;
     bool stop = false;  // this warp gave up on a copy (warp-uniform)
     (void)warp;
     for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
@@ -2044,8 +2131,12 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
         chunk_range(a.vocab, S, seg, c0, c1);
         const uint32_t ntiles = (c1 - c0 + TC - 1) / TC;
         Q38S_TT(u, 0);
-        Row r;
-        load_row(a, v, r);
+        // one copy of the row context per CTA, in shared memory: it is
+        // needed in the row's tail, and registers are scarce in the stream
+        // loop (every consumer finished the previous unit at its last barrier)
+        if (tid == 0) load_row(a, v, rs);
+        cbar();
+        const Row& r = rs;
         Q38S_TT(u, 1);
         const bool streams = unit_streams(a, v, c1 - c0, TC);
         const unsigned char* src_row = row_ptr<DT>(a, v);
@@ -2071,7 +2162,7 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
 #ifdef Q38S_TRACE
             const long long tw0 = clock64();
 #endif
-            bool ok = !stop && wait_full(c, slot, (g / kRing) & 1u, tile_wait);
+            bool ok = !stop && wait_full(a, c, slot, (g / kRing) & 1u);
 #ifdef Q38S_TRACE
             const long long tw1 = clock64();
 #endif
@@ -2545,6 +2636,35 @@ void set_stream_fault(uint32_t withhold, long long wait_cycles) {
     g_fault_wait = wait_cycles;
 }
 
+// The general kernel behind every stream kernel, as its programmatic
+// dependent (the launch overlaps the stream kernel).
+template <int DT>
+static cudaError_t launch_general(const SampleArgs& a, void* stream, int sms) {
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        e = cudaFuncSetAttribute(general_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kArea + kStageBytes));
+        if (e != cudaSuccess) return e;
+        configured[dev] = true;
+    }
+    const uint32_t grid = a.vrows < static_cast<uint32_t>(sms) ? a.vrows : static_cast<uint32_t>(sms);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kCons);
+    cfg.dynamicSmemBytes = kArea + kStageBytes;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, general_kernel<DT>, a);
+}
+
 template <int DT>
 static int launch_stream_t(const SampleArgs& a_in, void* stream) {
     SampleArgs a = a_in;
@@ -2580,7 +2700,8 @@ static int launch_stream_t(const SampleArgs& a_in, void* stream) {
     const uint32_t grid = units < cap ? units : cap;
     if (a.segs == 1) {
         kern<<<grid, kBlock, smem, static_cast<cudaStream_t>(stream)>>>(a);
-        return cudaGetLastError();
+        e = cudaGetLastError();
+        return e != cudaSuccess ? e : launch_general<DT>(a, stream, sms[dev]);
     }
     // one cluster of segs CTAs per row: CTA rank = segment
     cudaLaunchConfig_t cfg = {};
@@ -2595,7 +2716,8 @@ static int launch_stream_t(const SampleArgs& a_in, void* stream) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, a);
+    e = cudaLaunchKernelEx(&cfg, kern, a);
+    return e != cudaSuccess ? e : launch_general<DT>(a, stream, sms[dev]);
 }
 
 int launch_stream(const SampleArgs& a, void* stream) {
