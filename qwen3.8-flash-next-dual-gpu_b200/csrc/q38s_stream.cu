@@ -1048,6 +1048,7 @@ static_assert(kGB * 12 <= kArea && kGL * 16 + (kGB + 1) * 4 <= kArea, "general-p
 struct GRow {
     const uint32_t* keys;  // exact key per column (padded to whole 16-byte groups)
     uint4* stage;          // the passes' cp.async slots (kStageBytes of shared memory)
+    Ctl* ctl;              // the CTA's control block
     uint32_t V, tok0;
     float M;               // the row maximum
     uint32_t minp_key;     // smallest key whose weight reaches min_p (0: no min-p)
@@ -1086,6 +1087,17 @@ __device__ __forceinline__ double g_weight(const GRow g, uint32_t key) {
 }
 __device__ __forceinline__ double g_bin_scale(uint32_t b) {
     return exp(-static_cast<double>(b) * 0.03125);
+}
+// A 64-bit shared-memory sum kept as two 32-bit words: 32-bit atomics, the
+// carry out of the low word added to the high word (exact).
+__device__ __forceinline__ void add_u64_split(uint32_t* w, unsigned long long m) {
+    const uint32_t lo = static_cast<uint32_t>(m), hi = static_cast<uint32_t>(m >> 32);
+    const uint32_t old = atomicAdd(&w[0], lo);
+    const uint32_t up = hi + (old + lo < old ? 1u : 0u);
+    if (up) atomicAdd(&w[1], up);
+}
+__device__ __forceinline__ unsigned long long get_u64_split(const uint32_t* w) {
+    return static_cast<unsigned long long>(w[0]) | (static_cast<unsigned long long>(w[1]) << 32);
 }
 
 // Exclusive prefix sum of doubles over the consumers in thread order.
@@ -1137,7 +1149,7 @@ __device__ __forceinline__ void cp_async_wait() {
 // last group is zero-filled past its end.  Warp-uniform round count.
 template <typename F>
 __device__ __forceinline__ void g_pass16(const unsigned char* src, uint64_t nbytes, uint4* stage,
-                                         F&& f) {
+                                         Ctl&, F&& f) {
     const uint32_t n16 = static_cast<uint32_t>((nbytes + 15) / 16);
     const uint32_t rounds = (n16 + kCons - 1) / kCons;
     auto issue = [&](uint32_t r) {
@@ -1166,7 +1178,7 @@ __device__ __forceinline__ void g_pass16(const unsigned char* src, uint64_t nbyt
 template <typename F>
 __device__ __forceinline__ void g_for_keys(const GRow g, F&& f) {
     g_pass16(reinterpret_cast<const unsigned char*>(g.keys), static_cast<uint64_t>(g.V) * 4, g.stage,
-             [&](uint32_t gi, const uint4& kv, bool) {
+             *g.ctl, [&](uint32_t gi, const uint4& kv, bool) {
                  const uint32_t c0 = gi * 4;
                  f(c0, kv.x, c0 < g.V);
                  f(c0 + 1, kv.y, c0 + 1 < g.V);
@@ -1185,6 +1197,10 @@ __device__ __forceinline__ uint32_t g_keys(const SampleArgs& a, const Row& r, co
     constexpr uint32_t es = DT == Q38S_DTYPE_BF16 ? 2u : 4u;
     constexpr uint32_t pv = 16u / es;
     uint32_t kmax = 0;
+    // the reciprocal of the temperature, correctly rounded, for the division
+    // of unpenalised logits (temperatures in [2^-30, 2^30])
+    const float rcp_t = __frcp_rn(r.p.temperature);
+    const bool rcp_ok = r.p.temperature >= 0x1p-30f && r.p.temperature <= 0x1p30f;
     auto group = [&](uint32_t q, const uint4& w) {
         const uint32_t col0 = q * pv;
         uint32_t pw = 0;  // penalised bits of the 32-column word holding the group
@@ -1202,9 +1218,19 @@ __device__ __forceinline__ uint32_t g_keys(const SampleArgs& a, const Row& r, co
                     count = (r.counts_row ? r.counts_row[col] : 0u) +
                             (pbm ? extra_count(r, a.col_begin + col) : ex);
             }
-            k[e] = col < V ? float_key(transform(vec_elem<DT>(w, static_cast<int>(e)), pen, count,
-                                                 r.p))
-                           : 0u;
+            float x = vec_elem<DT>(w, static_cast<int>(e));
+            float v;
+            const float ax = fabsf(x);
+            if (!pen && ax <= 0x1p60f && (ax >= 0x1p-60f || ax == 0.0f)) {
+                // x / T by the reciprocal and one Markstein correction step
+                // (exact in this range for the temperature range checked below)
+                const float q0 = __fmul_rn(x, rcp_t);
+                v = __fmaf_rn(__fmaf_rn(-q0, r.p.temperature, x), rcp_t, q0);
+                if (!rcp_ok) v = __fdiv_rn(x, r.p.temperature);
+            } else {
+                v = transform(x, pen, count, r.p);
+            }
+            k[e] = col < V ? float_key(v) : 0u;
             kmax = max(kmax, k[e]);
         }
         if (col0 + pv <= V) {
@@ -1220,7 +1246,7 @@ __device__ __forceinline__ uint32_t g_keys(const SampleArgs& a, const Row& r, co
         }
     };
     if (a.use_tma) {
-        g_pass16(row, static_cast<uint64_t>(V) * es, stage, [&](uint32_t q, const uint4& w, bool valid) {
+        g_pass16(row, static_cast<uint64_t>(V) * es, stage, c, [&](uint32_t q, const uint4& w, bool valid) {
             if (valid) group(q, w);
         });
     } else {
@@ -1237,11 +1263,12 @@ __device__ __forceinline__ uint32_t g_keys(const SampleArgs& a, const Row& r, co
 __device__ __forceinline__ uint32_t g_level1(const GRow g, bool weighted, unsigned char* area, uint32_t* pc,
                              double* pm, double* Z, Ctl& c) {
     uint32_t* hc = reinterpret_cast<uint32_t*>(area);
-    unsigned long long* hm = reinterpret_cast<unsigned long long*>(area + kGB * 4);
+    uint32_t* hm = reinterpret_cast<uint32_t*>(area + kGB * 4);  // kGB split 64-bit sums
     cbar();
     for (uint32_t i = threadIdx.x; i < kGB; i += kCons) {
         hc[i] = 0;
-        hm[i] = 0;
+        hm[2 * i] = 0;
+        hm[2 * i + 1] = 0;
     }
     cbar();
     g_for_keys(g, [&](uint32_t col, uint32_t key, bool valid) {
@@ -1249,7 +1276,7 @@ __device__ __forceinline__ uint32_t g_level1(const GRow g, bool weighted, unsign
         float d;
         const uint32_t b = g_bin(g, key, d);
         atomicAdd(&hc[b], 1u);
-        if (weighted) atomicAdd(&hm[b], g_tw(d, b));
+        if (weighted) add_u64_split(&hm[2 * b], g_tw(d, b));
     });
     cbar();
     constexpr uint32_t kPer = kGB / kCons;
@@ -1259,7 +1286,8 @@ __device__ __forceinline__ uint32_t g_level1(const GRow g, bool weighted, unsign
     for (uint32_t j = 0; j < kPer; ++j) {
         const uint32_t b = threadIdx.x * kPer + j;
         lc[j] = hc[b];
-        lm[j] = (weighted && hm[b]) ? g_bin_scale(b) * (static_cast<double>(hm[b]) / kGUnit) : 0.0;
+        const unsigned long long mb = weighted ? get_u64_split(&hm[2 * b]) : 0ull;
+        lm[j] = mb ? g_bin_scale(b) * (static_cast<double>(mb) / kGUnit) : 0.0;
         sc += lc[j];
         sm += lm[j];
     }
@@ -1501,11 +1529,12 @@ __device__ __forceinline__ GLoc g_locate(const GRow g, const uint32_t* pc, const
         const int sh = span > kGB - 1 ? (32 - __clz(span)) - 11 : 0;
         const uint32_t top = span >> sh;
         uint32_t* hc = reinterpret_cast<uint32_t*>(area);
-        unsigned long long* hm = reinterpret_cast<unsigned long long*>(area + kGB * 4);
+        uint32_t* hm = reinterpret_cast<uint32_t*>(area + kGB * 4);  // split 64-bit sums
         cbar();
         for (uint32_t i = threadIdx.x; i < kGB; i += kCons) {
             hc[i] = 0;
-            hm[i] = 0;
+            hm[2 * i] = 0;
+            hm[2 * i + 1] = 0;
         }
         cbar();
         g_for_keys(g, [&](uint32_t col, uint32_t key, bool valid) {
@@ -1515,7 +1544,7 @@ __device__ __forceinline__ GLoc g_locate(const GRow g, const uint32_t* pc, const
             if (mass) {
                 float d;
                 g_bin(g, key, d);
-                atomicAdd(&hm[sb], g_tw(d, s.b1));
+                add_u64_split(&hm[2 * sb], g_tw(d, s.b1));
             }
         });
         cbar();
@@ -1525,7 +1554,7 @@ __device__ __forceinline__ GLoc g_locate(const GRow g, const uint32_t* pc, const
         for (uint32_t j = 0; j < kPer; ++j) {
             const uint32_t b = threadIdx.x * kPer + j;
             lc[j] = hc[b];
-            lm[j] = mass ? scale * (static_cast<double>(hm[b]) / kGUnit) : 0.0;
+            lm[j] = mass ? scale * (static_cast<double>(get_u64_split(&hm[2 * b])) / kGUnit) : 0.0;
             sc += lc[j];
             sm += lm[j];
         }
@@ -1617,7 +1646,7 @@ __device__ __forceinline__ void g_write_tie(const GRow g, const GOut o, uint32_t
     const float val = key_float(key);
     const double w = g_weight(g, key);
     g_pass16(reinterpret_cast<const unsigned char*>(g.keys), static_cast<uint64_t>(g.V) * 4, g.stage,
-             [&](uint32_t gi, const uint4& kv, bool) {
+             c, [&](uint32_t gi, const uint4& kv, bool) {
                  const uint32_t kk[4] = {kv.x, kv.y, kv.z, kv.w};
                  uint32_t flags = 0;
 #pragma unroll
@@ -1809,6 +1838,7 @@ __device__ __forceinline__ void general_row(const SampleArgs& a, const Row& r, u
     GRow g;
     g.keys = keys;
     g.stage = stage;
+    g.ctl = &c;
     g.V = V;
     g.tok0 = tok0;
     const uint32_t M_key = g_keys<DT>(a, r, row, pbm, keys, V, g.stage, c);
