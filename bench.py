@@ -9,14 +9,20 @@ heterogeneous per-row parameters (temperature, top_k 0 or 1..100, top_p,
 min_p, repetition penalty) and per-row histories of 1..32,768 tokens.  A
 step is one q38s_batch_sample_commit call: prepare (penalties, temperature,
 top-k, min-p, top-p, seeded draw) plus commit of the decision and of the
-sampled token, for all 256 rows.  Inputs rotate over 4 distinct batches
-(311 MB > the 126 MB L2), so every step reads its logits from HBM.
+sampled token, for all 256 rows.  Inputs rotate over distinct batches
+(more than 320 MB per GPU > the 126 MB L2), so every step reads its logits
+from HBM.
 
-N > 1 (torchrun, one process per GPU): every rank runs its own 256-row batch
-(row sharding, no collective on the data path; weak scaling), and the line
-adds configuration 5 (vocab-parallel sampling: 1,024 fp32 rows split
-column-wise over the N GPUs, local top-64, all-gather of the candidates,
-merge and draw).
+N > 1 (torchrun, one process per GPU): the 256 rows are split into
+contiguous blocks of 256 / N rows, one per GPU, with no collective on the
+data path (strong scaling: the headline value).  The line adds weak scaling
+(every GPU its own 256 rows) and configuration 5 (vocab-parallel sampling:
+1,024 fp32 rows split column-wise over the N GPUs, local top-64, all-gather
+of the candidates, merge and draw, with each phase's time).
+
+N = 1 adds configuration 2 (batch-1 latency), configuration 3 (speculative
+verification), configuration 4 over eight parameter draws, and the CPU
+baseline.
 
 --impl reference times the reference's own CPU implementation
 (src/sampling.cc compiled unmodified into oracle/_ref/libq38ref.so, one
@@ -134,6 +140,26 @@ def bf16_tensor(arr, dev):
     return torch.from_numpy(arr.view(np.int16)).to(dev).view(torch.bfloat16)
 
 
+def device_cfg4_logits(rows: int, seed: int, dev):
+    """A batch with the configuration-4 row distribution generated on the
+    GPU (seeded): bf16 N(0, 2.5^2) with 32 spikes per row at distinct random
+    columns, the spike of Zipf rank k at 15 - 1.1 ln k."""
+    import torch
+    g = torch.Generator(dev).manual_seed(seed)
+    x = torch.randn((rows, VOCAB), device=dev, generator=g) * 2.5
+    cols = torch.rand((rows, VOCAB), device=dev, generator=g).topk(32, dim=1).indices
+    ranks = torch.arange(1, 33, device=dev, dtype=torch.float32)
+    x.scatter_(1, cols, (15.0 - 1.1 * torch.log(ranks)).expand(rows, 32).contiguous())
+    return x.to(torch.bfloat16)
+
+
+def input_batches(rows: int, seed: int, dev, min_bytes: float = 320e6):
+    """Distinct input batches whose rotation exceeds the 126 MB L2 (and at
+    least four)."""
+    n = max(N_INPUT_BATCHES, int(np.ceil(min_bytes / (rows * ROW_BYTES_BF16))))
+    return [device_cfg4_logits(rows, seed * 1000 + b, dev) for b in range(n)]
+
+
 def time_steps(step_fns, steps, stream, graph_len=32):
     """Runs `steps` steps (step i calls step_fns[i % len]) as CUDA graphs of
     graph_len steps plus one graph of the remainder; returns elapsed ms
@@ -185,56 +211,46 @@ def run_ours(args, rank, world, dist):
     stream = torch.cuda.Stream(dev)
     peak, peak_kind = load_peaks()
 
-    # ---- configuration 4 on this rank (weak scaling: own 256 rows).  Every
-    # rank samples the same row specification (parameters, histories: the
-    # single-GPU draw) on its own logits, so each GPU does the same work.
+    # ---- configuration 4, strong scaling (the headline): the 256 rows of the
+    # seed-4 draw split into contiguous blocks, rank r samples rows
+    # [r * 256 / N, (r + 1) * 256 / N) on its own GPU; no collective.
     spec = synth.cfg4_spec(seed=4)
     configs = cfg4_configs(q38s, spec)
-    batch = q38s.Batch(VOCAB, configs, device=dev.index)
-    batch.commit_tokens(spec.histories)
-    host_batches = [synth.cfg4_logits(batch=b, seed=4 + 1000 * rank) for b in range(N_INPUT_BATCHES)]
-    inputs = [bf16_tensor(h, dev) for h in host_batches]
-    decisions = [batch.decisions_buffer() for _ in range(N_INPUT_BATCHES)]
-    fns = [lambda s, i=i: batch.sample_commit(inputs[i], decisions[i], stream=s)
-           for i in range(N_INPUT_BATCHES)]
-
-    with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            fns[i % N_INPUT_BATCHES](stream)
-    torch.cuda.synchronize()
+    lo, hi = rank * ROWS // world, (rank + 1) * ROWS // world
+    rows_local = hi - lo
+    inputs = input_batches(rows_local, 4 + 1000 * rank, dev)
     clocks = ClockSampler(dev.index)
     clocks.start()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ms = time_steps(fns, args.steps, stream)
-    torch.cuda.synchronize()
-    # keep the GPU under the same load until a few clock samples exist
-    soak_t0 = time.time()
-    while "cpu" in args.workloads and time.time() - soak_t0 < 1.2:
-        time_steps(fns, 2048, stream)
+    batch, decisions, ms_max, ms = cfg4_measure(q38s, configs[lo:hi], spec.histories[lo:hi],
+                                                inputs, args, dev, stream, dist)
+    soak_t0 = time.time()  # keep the GPU under load until a few clock samples exist
+    while time.time() - soak_t0 < 1.2:
+        cfg4_replay(batch, decisions, inputs, stream, 2048)
     clk = clocks.stop()
-    if dist:
-        dist.barrier()
-    ms_max = ms
-    if dist:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
     st = batch.decode_decisions(decisions[0])
     assert (st["status"] == 0).all(), "sampler reported a row error"
-
     ms_per_step = ms_max / args.steps
-    rows_total = ROWS * world
+    rows_total = ROWS
     value = rows_total / (ms_per_step / 1e3)
-    algo_bytes = ROWS * ROW_BYTES_BF16
+    algo_bytes = rows_local * ROW_BYTES_BF16
     achieved = algo_bytes / (ms / args.steps / 1e3) / 1e9
+
+    # weak scaling, an extra key at N > 1: every rank its own 256 rows
+    weak = None
+    if world > 1:
+        winputs = input_batches(ROWS, 7 + 1000 * rank, dev)
+        wb, wd, wms_max, _ = cfg4_measure(q38s, configs, spec.histories, winputs, args, dev,
+                                          stream, dist)
+        weak = {"value": ROWS * world / (wms_max / args.steps / 1e3), "unit": "rows/s",
+                "ms_per_step": wms_max / args.steps, "rows_per_gpu": ROWS,
+                "scaling": "weak"}
+        del wb, wd, winputs
 
     # ---- end to end: pinned host logits -> device -> sample -> host decisions
     e2e_steps = max(3, min(40, args.steps))
-    pinned = [torch.from_numpy(h.view(np.int16)).pin_memory() for h in host_batches[:2]]
-    dev_in = torch.empty((ROWS, VOCAB), dtype=torch.int16, device=dev)
-    host_dec = torch.empty(ROWS * 3, dtype=torch.int64).pin_memory()
+    pinned = [inputs[i].view(torch.int16).cpu().pin_memory() for i in range(2)]
+    dev_in = torch.empty((rows_local, VOCAB), dtype=torch.int16, device=dev)
+    host_dec = torch.empty(rows_local * 3, dtype=torch.int64).pin_memory()
     with torch.cuda.stream(stream):
         for _ in range(2):
             dev_in.copy_(pinned[0], non_blocking=True)
@@ -269,44 +285,112 @@ def run_ours(args, rank, world, dist):
         "warmup": args.warmup,
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded; q38s.synth cfg4: N(0,2.5^2) + Zipf(1.1)-ranked spikes)",
-        "config": {"workload": "cfg4 batched serving: 256 rows x 151,936 bf16 per GPU, "
+        "data": "synthetic (seeded on the GPU: N(0,2.5^2) bf16 + Zipf(1.1)-ranked spikes, the "
+                "cfg4 distribution; row parameters and histories from q38s.synth.cfg4_spec(4))",
+        "config": {"workload": "cfg4 batched serving: 256 rows x 151,936 bf16 in total, "
                                "heterogeneous T/top_k/top_p/min_p/repetition, histories "
                                "U{1..32768}; step = prepare + commit + commit_token",
-                   "rows_per_gpu": ROWS, "vocab": VOCAB, "global_batch": rows_total,
-                   "parallelism": f"row-sharded x{world} (no collective)",
-                   "rows": "every rank: the same row parameters and histories (seed 4), "
-                           "its own logits (seed 4 + 1000 * rank)",
-                   "l2": f"inputs rotate over {N_INPUT_BATCHES} batches "
-                         f"({N_INPUT_BATCHES * ROWS * ROW_BYTES_BF16 / 1e6:.0f} MB > 126 MB L2)",
+                   "rows_per_gpu": rows_local, "vocab": VOCAB, "global_batch": rows_total,
+                   "parallelism": f"row-sharded x{world}: contiguous blocks of "
+                                  f"{rows_local} rows, no collective",
+                   "l2": f"inputs rotate over {len(inputs)} batches "
+                         f"({len(inputs) * rows_local * ROW_BYTES_BF16 / 1e6:.0f} MB per GPU "
+                         "> 126 MB L2)",
                    "timing": "CUDA graphs of 32 steps, CUDA events on the launch stream, "
                              "max over ranks"},
         "hbm_gbs": achieved,
         "e2e": {"value": rows_total / (e2e_ms / 1e3), "unit": "rows/s",
-                "h2d_bytes_per_step": ROWS * ROW_BYTES_BF16,
-                "d2h_bytes_per_step": ROWS * 24,
+                "h2d_bytes_per_step": rows_total * ROW_BYTES_BF16,
+                "d2h_bytes_per_step": rows_total * 24,
                 "path": "pinned host logits -> cudaMemcpyAsync -> q38s_batch_sample_commit "
-                        "-> decisions to pinned host, stream sync each step"},
-        "gpu_launches": args.steps,
+                        "-> decisions to pinned host, stream sync each step (bytes summed "
+                        "over ranks)"},
+        "gpu_launches": 2 * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "frac_of_8tbs_nominal": achieved / 8000.0,
                      "traffic": load_traffic("cfg4_stream_kernel_bf16"),
-                     "kernel": "stream_kernel<bf16> (one launch per step)",
+                     "kernel": "stream_kernel<bf16> (one launch per step, plus the general "
+                               "kernel behind it, which returns at once when no row is "
+                               "deferred)",
                      "algorithmic_bytes_per_launch": algo_bytes},
         "clocks": clk,
     }
+    if weak is not None:
+        line["weak_scaling"] = weak
 
     if world == 1:
         line.update(extra_single_gpu(args, dev, stream))
+        if "draws" in args.workloads:
+            line["cfg4_draws"] = cfg4_draws(q38s, dev, stream)
         if "cpu" in args.workloads:
-            line["cpu_baseline"] = cpu_baseline(spec, host_batches[0])
+            host0 = inputs[0].view(torch.int16).cpu().numpy().view(np.uint16)
+            line["cpu_baseline"] = cpu_baseline(spec, host0)
     elif "cfg5" in args.workloads:
         line["vocab_parallel"] = vocab_parallel(args, rank, world, dev, stream, dist)
     return line
+
+
+def cfg4_replay(batch, decisions, inputs, stream, steps):
+    fns = [lambda s, i=i: batch.sample_commit(inputs[i], decisions[i % len(decisions)], stream=s)
+           for i in range(len(inputs))]
+    return time_steps(fns, steps, stream)
+
+
+def cfg4_measure(q38s, configs, histories, inputs, args, dev, stream, dist):
+    """args.warmup + args.steps sample-commit steps of a batch over the
+    rotating inputs; returns (batch, decisions, max-over-ranks ms, own ms)."""
+    import torch
+    batch = q38s.Batch(VOCAB, configs, device=dev.index)
+    batch.commit_tokens(histories)
+    decisions = [batch.decisions_buffer() for _ in range(N_INPUT_BATCHES)]
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            batch.sample_commit(inputs[i % len(inputs)], decisions[i % N_INPUT_BATCHES],
+                                stream=stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = cfg4_replay(batch, decisions, inputs, stream, args.steps)
+    torch.cuda.synchronize()
+    ms_max = ms
+    if dist:
+        dist.barrier()
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    return batch, decisions, ms_max, ms
+
+
+def cfg4_draws(q38s, dev, stream, draws=range(4, 12), steps=1024):
+    """Configuration 4 over eight parameter draws (row parameters and
+    histories of q38s.synth.cfg4_spec(seed)), 1,024 consecutive sample-commit
+    steps each: the mean step time per draw and the slowest 32-step stretch."""
+    import torch
+    inputs = input_batches(ROWS, 11, dev)
+    per_draw, worst = [], []
+    for seed in draws:
+        spec = synth.cfg4_spec(seed=seed)
+        batch = q38s.Batch(VOCAB, cfg4_configs(q38s, spec), device=dev.index)
+        batch.commit_tokens(spec.histories)
+        decisions = [batch.decisions_buffer() for _ in range(N_INPUT_BATCHES)]
+        cfg4_replay(batch, decisions, inputs, stream, 32)
+        chunks = [cfg4_replay(batch, decisions, inputs, stream, 32) * 1e3 / 32
+                  for _ in range(steps // 32)]
+        per_draw.append(float(np.mean(chunks)))
+        worst.append(float(np.max(chunks)))
+        st = batch.decode_decisions(decisions[0])
+        assert (st["status"] == 0).all(), f"draw {seed}: a row error"
+        del batch, decisions
+        torch.cuda.synchronize()
+    return {"draws": list(draws), "steps_per_draw": steps,
+            "us_per_step_by_draw": per_draw,
+            "min_us": min(per_draw), "median_us": float(np.median(per_draw)),
+            "max_us": max(per_draw), "slowest_32_step_stretch_us": max(worst)}
 
 
 def extra_single_gpu(args, dev, stream):
@@ -374,15 +458,17 @@ def batch1_latency(dev, stream):
         raise RuntimeError(f"native batch-1 latency harness failed ({rc})")
     nlat.sort()
     nrank = lambda q: nlat[max(0, int(np.ceil(n_steps * q / 100.0)) - 1)]
-    # device time of the same kernel, batch of 1 row, events over 2,000 calls
+    # device time of the same kernels, batch of 1 row, events over 2,400
+    # calls rotating through the 600 pool rows (182 MB > L2)
     b1 = q38s.Batch(VOCAB, [cfg], device=dev.index)
     b1.commit_tokens([synth.cfg2_history()])
     dec = b1.decisions_buffer()
-    fns = [lambda st, i=i: b1.sample_commit(pool[i:i + 1], dec, stream=st) for i in range(8)]
+    fns = [lambda st, i=i: b1.sample_commit(pool[i:i + 1], dec, stream=st)
+           for i in range(pool_n)]
     with torch.cuda.stream(stream):
-        for f in fns:
+        for f in fns[:8]:
             f(stream)
-    dev_ms = time_steps(fns, 2000, stream) / 2000
+    dev_ms = time_steps(fns, 4 * pool_n, stream) / (4 * pool_n)
     out["batch1"] = {"config": "cfg2: 1 row bf16, T 0.6, top_k 20, top_p 0.95, min_p 0, "
                                "presence 0.5, history 8,192 -> 18,192, 10,000 calls",
                      "p50_us": float(nrank(50)), "p99_us": float(nrank(99)),
@@ -395,6 +481,8 @@ def batch1_latency(dev, stream):
                                 "mean_us": float(lat.mean()),
                                 "call": "q38s.Sampler.prepare_device (ctypes), same loop"},
                      "device_us": dev_ms * 1e3,
+                     "device_timing": "q38s_batch_sample_commit on one row, CUDA graphs, "
+                                      "rows rotating through 182 MB (> L2)",
                      "target_us": 20.0}
     return out
 
@@ -406,38 +494,53 @@ def mtp_bench(dev, stream):
 
     out = {}
     c3 = synth.CFG3
-    tgt, drf = synth.cfg3_rows()
     cfg3 = q38s.config_v2(top_k=c3["top_k"], top_p=c3["top_p"], temperature=c3["temperature"],
                           seed=c3["seed"])
     b3 = q38s.Batch(VOCAB, [cfg3], device=dev.index)
-    t_t = torch.from_numpy(tgt).to(dev)
-    d_t = torch.from_numpy(drf).to(dev)
-    # draft tokens sampled from the draft distributions by the engine itself
+    # two input sets (158 MB > L2), each with draft tokens sampled from its
+    # draft distributions by the engine itself
     bq = q38s.Batch(VOCAB, [q38s.config_v2(top_k=20, top_p=0.95, temperature=0.7,
                                            seed=1000 + i) for i in range(64)], device=dev.index)
-    dq = bq.decode_decisions(bq.prepare(d_t[:64]))
-    drafts = torch.from_numpy(dq["token"].astype(np.int32)).to(dev)
+    sets = []
+    for seed in (3, 4):
+        tgt, drf = synth.cfg3_rows(seed=seed)
+        t_t = torch.from_numpy(tgt).to(dev)
+        d_t = torch.from_numpy(drf).to(dev)
+        dq = bq.decode_decisions(bq.prepare(d_t[:64]))
+        sets.append((t_t, d_t, torch.from_numpy(dq["token"].astype(np.int32)).to(dev)))
     res = torch.zeros(q38s.C.sizeof(q38s.MtpResult), dtype=torch.uint8, device=dev)
-    fns = [lambda st: b3.mtp_verify(0, t_t, d_t[:64], drafts, result=res, stream=st)]
+    fns = [lambda st, x=x: b3.mtp_verify(0, x[0], x[1][:64], x[2], result=res, stream=st)
+           for x in sets]
     with torch.cuda.stream(stream):
-        for _ in range(5):
-            fns[0](stream)
+        for _ in range(4):
+            for f in fns:
+                f(stream)
     torch.cuda.synchronize()
     mtp_ms = time_steps(fns, 200, stream, graph_len=8) / 200
+    accepted = []
+    for f in fns:
+        with torch.cuda.stream(stream):
+            f(stream)
+        stream.synchronize()
+        accepted.append(int(b3.decode_mtp(res).n_accepted))
     r = b3.decode_mtp(res)
     mtp_bytes = 129 * ROW_BYTES_F32
     out["mtp_verify"] = {"config": "cfg3: 65 target + 64 draft rows x 151,936 fp32, top_k 20, "
                                    "top_p 0.95, T 0.7",
-                         "us": mtp_ms * 1e3, "accepted": int(r.n_accepted),
+                         "us": mtp_ms * 1e3, "accepted_by_set": accepted,
                          "published": int(r.n_tokens), "status": int(r.status),
                          "hbm_gbs": mtp_bytes / (mtp_ms / 1e3) / 1e9,
                          "algorithmic_bytes": mtp_bytes,
-                         "l2": "same 79 MB every call (fits L2)"}
+                         "l2": "two input sets alternate (158 MB > 126 MB L2)"}
     return out
 
 
 def vocab_parallel(args, rank, world, dev, stream, dist):
-    """Configuration 5: 1,024 fp32 rows, columns split over the ranks."""
+    """Configuration 5: 1,024 fp32 rows of the cfg4 distribution, columns
+    split over the ranks: local top-64 (q38s_shard_topk), NCCL all-gather of
+    the (value, token) lists, merge and draw (q38s_shard_merge_sample) on
+    every rank.  Step time (max over ranks) and each phase's CUDA-event time;
+    every rank must draw the same tokens."""
     import torch
     import q38s
 
@@ -449,17 +552,28 @@ def vocab_parallel(args, rank, world, dev, stream, dist):
                               seed=int(spec.seed[r])) for r in range(rows)]
     sb = q38s.Batch(VOCAB, configs, device=dev.index, shard=(col0, w))
     sb.commit_tokens([h[(h >= col0) & (h < col0 + w)] for h in spec.histories])
-    gen = torch.Generator(dev).manual_seed(5 + rank)
-    shard = (torch.randn((rows, w), device=dev, generator=gen) * 2.5).contiguous()
+    host = np.empty((rows, w), np.float32)
+    for r in range(rows):
+        host[r] = synth.cfg5_row(r)[col0:col0 + w]
+    shard = torch.from_numpy(host).to(dev)
     local = torch.zeros(rows * k * 2, dtype=torch.int32, device=dev)
     gathered = torch.zeros(world * rows * k * 2, dtype=torch.int32, device=dev)
     dec = sb.decisions_buffer()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
 
-    def step():
+    def step(timed=False):
+        if timed:
+            ev[0].record(stream)
         sb.shard_topk(shard, k, out=local, stream=stream)
+        if timed:
+            ev[1].record(stream)
         with torch.cuda.stream(stream):
             dist.all_gather_into_tensor(gathered, local)
+        if timed:
+            ev[2].record(stream)
         sb.shard_merge_sample(gathered, world, k, decisions=dec, stream=stream)
+        if timed:
+            ev[3].record(stream)
 
     for _ in range(3):
         step()
@@ -474,16 +588,35 @@ def vocab_parallel(args, rank, world, dev, stream, dist):
     e1.record(stream)
     e1.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    # per phase, over 20 separately timed steps
+    phases = [[], [], []]
+    for _ in range(20):
+        step(timed=True)
+        ev[3].synchronize()
+        for i in range(3):
+            phases[i].append(ev[i].elapsed_time(ev[i + 1]) * 1e3)
+    t = torch.tensor([ms] + [float(np.median(p)) for p in phases], device=dev,
+                     dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms, topk_us, gather_us, merge_us = [float(x) for x in t.tolist()]
     st = sb.decode_decisions(dec)
-    return {"config": f"cfg5: 1,024 rows x 151,936 fp32, {world} column shards of {w}, "
-                      "local top-64, NCCL all-gather of (value, token), merge, top_p 0.9",
+    # the same tokens on every rank (same candidates, same seeds)
+    tok = torch.from_numpy(st["token"].astype(np.int64)).to(dev)
+    lo_t, hi_t = tok.clone(), tok.clone()
+    dist.all_reduce(lo_t, op=dist.ReduceOp.MIN)
+    dist.all_reduce(hi_t, op=dist.ReduceOp.MAX)
+    identical = bool(torch.equal(lo_t, hi_t))
+    return {"config": f"cfg5: 1,024 rows x 151,936 fp32 (cfg4 distribution, q38s.synth.cfg5_row), "
+                      f"{world} column shards of {w}, local top-64, NCCL all-gather of "
+                      "(value, token), merge, top_p 0.9",
             "rows_per_s": rows / (ms / 1e3), "ms_per_step": ms,
+            "phase_us": {"shard_topk": topk_us, "all_gather": gather_us,
+                         "shard_merge_sample": merge_us},
             "hbm_gbs_per_gpu": rows * w * 4 / (ms / 1e3) / 1e9,
             "row_errors": int((st["status"] != 0).sum()),
-            "collective": "torch.distributed all_gather_into_tensor (NCCL)"}
+            "tokens_identical_across_ranks": identical,
+            "collective": "torch.distributed all_gather_into_tensor (NCCL), launches issued "
+                          "eagerly"}
 
 
 def cpu_baseline(spec, logits_bf16, budget_s: float = 12.0):
@@ -554,7 +687,7 @@ def run_reference(args, rank, world):
     return {"impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "cfg4 batched serving rows (256 x 151,936 bf16, "
                                    "heterogeneous); reference prepare() per row",
                        "rows_per_step": len(sub)},
@@ -572,7 +705,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workloads", default="cfg4,cfg2,cfg3,cfg5,cpu",
+    ap.add_argument("--workloads", default="cfg4,cfg2,cfg3,cfg5,draws,cpu",
                     help="comma list of the measurements to run (cfg4 always runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

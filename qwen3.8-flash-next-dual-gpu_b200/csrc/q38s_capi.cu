@@ -490,6 +490,7 @@ int q38s_shard_merge_sample(const q38s_batch* b, const q38s_candidate* gathered,
     if (!b || !gathered || !decisions) return fail(Q38S_INVALID_ARGUMENT, "null argument");
     if (n_shards == 0 || k_local == 0 || static_cast<uint64_t>(n_shards) * k_local > 4096)
         return fail(Q38S_INVALID_ARGUMENT, "n_shards * k_local must be in [1, 4096]");
+    if (n_shards > 64) return fail(Q38S_INVALID_ARGUMENT, "at most 64 column shards");
     if (b->any_greedy) return fail(Q38S_LOGIC_ERROR, kMsgGreedy);
     for (uint32_t r = 0; r < b->rows; ++r)
         if (b->configs[r].top_k == 0 || b->configs[r].top_k > k_local)
@@ -675,6 +676,7 @@ int prepare_common(const q38s_sampler* cs, const void* d_logits, uint16_t dtype,
     // read-back copy and no stream synchronisation on the common path.
     a.decisions = s->d_decision;
     a.decisions_host = 1;
+    a.host_general = 1;   // the general kernel only for a deferred row (below)
     a.rng_from_args = 1;  // the committed state lives on the host
     a.rng_state = s->state.rng_state;
     if (n_extra) {
@@ -686,13 +688,26 @@ int prepare_common(const q38s_sampler* cs, const void* d_logits, uint16_t dtype,
     hd->status = kStatusPending;
     rc = launch_checked(a, s->stream, "prepare", s->batch->device);
     if (rc) return rc;
-    const auto t_start = std::chrono::steady_clock::now();
-    for (uint32_t spin = 1; hd->status == kStatusPending; ++spin) {
-        if ((spin & 1023u) == 0 &&
-            std::chrono::steady_clock::now() - t_start > std::chrono::milliseconds(200))
-            break;  // long or failed: the stream reports it
+    auto wait_decision = [&]() -> int {
+        const auto t_start = std::chrono::steady_clock::now();
+        for (uint32_t spin = 1; hd->status == kStatusPending; ++spin) {
+            if ((spin & 1023u) == 0 &&
+                std::chrono::steady_clock::now() - t_start > std::chrono::milliseconds(200))
+                break;  // long or failed: the stream reports it
+        }
+        if (hd->status == kStatusPending) Q38S_CUDA(cudaStreamSynchronize(s->stream), "prepare");
+        return Q38S_OK;
+    };
+    rc = wait_decision();
+    if (rc) return rc;
+    if (hd->status == kRowDeferred) {
+        // the row needs the general path: its kernel, then the decision
+        hd->status = kStatusPending;
+        const int e = launch_general_only(a, s->stream);
+        if (e != cudaSuccess) return cuda_fail(static_cast<cudaError_t>(e), "prepare");
+        rc = wait_decision();
+        if (rc) return rc;
     }
-    if (hd->status == kStatusPending) Q38S_CUDA(cudaStreamSynchronize(s->stream), "prepare");
     q38s_decision_v1 d;
     d.token = hd->token;
     d.status = hd->status;

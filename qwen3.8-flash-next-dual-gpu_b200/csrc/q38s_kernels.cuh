@@ -87,6 +87,10 @@ struct SampleArgs {
     // deferred[v] != 0: virtual row v takes the general path (general
     // kernel); zero between launches (vrows words)
     uint32_t* deferred;
+    // host_general: the caller launches the general kernel itself, only when
+    // a row reports kRowDeferred (the one-session sampler, which waits for
+    // its decision anyway); otherwise it runs behind every stream kernel
+    int host_general;
     // speculative verification, run by the last row to finish
     q38s_mtp_result* mtp;
     uint32_t n_draft;
@@ -109,8 +113,13 @@ struct SampleArgs {
 // cluster size; above it the kernel allows non-portable sizes).
 constexpr uint32_t kMaxSegs = 8;
 
+// Decision status of a row handed to the general kernel when the caller
+// launches that kernel itself (host_general); never returned to users.
+constexpr int32_t kRowDeferred = 100;
+
 // Launchers (q38s_stream.cu, q38s_sample.cu).  All return a cudaError_t as int.
 int launch_stream(const SampleArgs& a, void* stream);   // streaming sampler
+int launch_general_only(const SampleArgs& a, void* stream);  // the deferred rows of a launch
 // Failure injection applied to every later stream-kernel launch of the
 // process (tests only; withhold 0 turns it off).
 void set_stream_fault(uint32_t withhold, long long wait_cycles);

@@ -39,43 +39,6 @@ __device__ __forceinline__ uint32_t block_min_u32(uint32_t v, Ctl& c) {
     __syncthreads();
     return r;
 }
-__device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, Ctl& c) {
-    v = warp_sum_u32(v);
-    const int w = threadIdx.x >> 5;
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) c.red_u32[w] = v;
-    __syncthreads();
-    uint32_t r = 0;
-    for (int i = 0; i < kThreads / 32; ++i) r += c.red_u32[i];
-    __syncthreads();
-    return r;
-}
-
-// Sorts keys[0..n) in descending order; n is a power of two; whole block.
-__device__ void bitonic_desc(uint64_t* keys, uint32_t n) {
-    for (uint32_t size = 2; size <= n; size <<= 1) {
-        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-            for (uint32_t i = threadIdx.x; i < n / 2; i += blockDim.x) {
-                const uint32_t lo = 2 * i - (i & (stride - 1));
-                const uint32_t hi = lo + stride;
-                const bool desc = (lo & size) == 0;
-                const uint64_t a = keys[lo], b = keys[hi];
-                if ((a < b) == desc) {
-                    keys[lo] = b;
-                    keys[hi] = a;
-                }
-            }
-            __syncthreads();
-        }
-    }
-}
-
-__device__ __forceinline__ uint32_t pow2_at_least(uint32_t n) {
-    uint32_t p = 1;
-    while (p < n) p <<= 1;
-    return p;
-}
-
 // Column partition: 128-column blocks spread over S CTAs.
 
 // Softmax / min-p / top-p / draw over `n` candidates sorted by rank key,
@@ -242,40 +205,65 @@ __global__ void reset_states_kernel(RowState* state, const uint64_t* seeds, uint
     state[row] = RowState{seeds[row], 0, 0, 0};
 }
 
+constexpr uint32_t kMaxShards = 64;  // column shards one merge takes
+
 // ------------------------------------------------ vocab-shard merge
-// One CTA per row: candidates of all shards -> global top-k (canonical
-// order) -> min-p / top-p / draw.
+// One CTA per row.  Each shard's list arrives sorted in canonical order
+// (value desc, token asc) with its invalid entries (token -1) at the end, and
+// tokens are distinct across shards, so an entry's position in the merged
+// order is its index in its own list plus, for every other shard, the number
+// of that shard's entries that rank above it (a binary search).  Entries
+// whose position is below the row's top-k are written to their place; no
+// sort is needed.  Then min-p / top-p / the draw (the stream kernel's
+// epilogue) over that prefix.
 __global__ void __launch_bounds__(kThreads) shard_merge_kernel(
     const RowParams* params, const RowState* state, const q38s_candidate* gathered,
     uint32_t rows, uint32_t n_shards, uint32_t k_local, q38s_decision_v1* decisions) {
     extern __shared__ __align__(16) unsigned char sm[];
     __shared__ Ctl c;
+    __shared__ uint32_t len[kMaxShards];
     const uint32_t row = blockIdx.x;
     const uint32_t total = n_shards * k_local;
-    const uint32_t p2 = pow2_at_least(total);
-    uint64_t* keys = reinterpret_cast<uint64_t*>(sm);
-    double* w = reinterpret_cast<double*>(sm + static_cast<size_t>(p2) * 8);
-    double* S = w + p2;
-    double* q = S + p2;
-    for (uint32_t i = threadIdx.x; i < p2; i += blockDim.x) {
-        uint64_t k = 0;
-        if (i < total) {
-            const uint32_t s = i / k_local, j = i % k_local;
-            const q38s_candidate cd =
-                gathered[(static_cast<size_t>(s) * rows + row) * k_local + j];
-            if (cd.token >= 0) k = rank_key(float_key(cd.value), static_cast<uint32_t>(cd.token));
-        }
-        keys[i] = k;
+    uint64_t* keys = reinterpret_cast<uint64_t*>(sm);         // [total], by shard
+    uint64_t* out = keys + total;                             // [k_local]: the merged prefix
+    double* w = reinterpret_cast<double*>(out + k_local);
+    double* S = w + k_local;
+    double* q = S + k_local;
+    if (threadIdx.x < n_shards) len[threadIdx.x] = 0;
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < total; i += blockDim.x) {
+        const uint32_t s = i / k_local, j = i % k_local;
+        const q38s_candidate cd = gathered[(static_cast<size_t>(s) * rows + row) * k_local + j];
+        const bool ok = cd.token >= 0;
+        keys[i] = ok ? rank_key(float_key(cd.value), static_cast<uint32_t>(cd.token)) : 0ull;
+        if (ok) atomicMax(&len[s], j + 1);  // valid entries form a prefix of the list
     }
     __syncthreads();
-    bitonic_desc(keys, p2);
     uint32_t valid = 0;
-    for (uint32_t i = threadIdx.x; i < total; i += blockDim.x) valid += keys[i] != 0;
-    valid = block_sum_u32(valid, c);
+    for (uint32_t s = 0; s < n_shards; ++s) valid += len[s];
     const RowParams p = params[row];
     const uint32_t keep = (p.top_k && p.top_k < valid) ? p.top_k : valid;
+    for (uint32_t i = threadIdx.x; i < total; i += blockDim.x) {
+        const uint32_t s = i / k_local, j = i % k_local;
+        if (j >= len[s]) continue;
+        const uint64_t x = keys[i];
+        uint32_t pos = j;
+        for (uint32_t s2 = 0; s2 < n_shards && pos < keep; ++s2) {
+            if (s2 == s) continue;
+            const uint64_t* l = keys + static_cast<size_t>(s2) * k_local;
+            uint32_t lo = 0, hi = len[s2];  // entries of l above x: the first index below x
+            while (lo < hi) {
+                const uint32_t mid = (lo + hi) >> 1;
+                if (l[mid] > x) lo = mid + 1;
+                else hi = mid;
+            }
+            pos += lo;
+        }
+        if (pos < keep) out[pos] = x;
+    }
+    __syncthreads();
     const uint64_t rb = state[row].rng_state;
-    epilogue(keys, keep, p, true, rb, w, S, q, c);
+    epilogue(out, keep, p, true, rb, w, S, q, c);
     if (threadIdx.x == 0) {
         q38s_decision_v1 d;
         d.token = c.e_status == Q38S_ROW_OK ? c.e_token : -1;
@@ -359,13 +347,19 @@ int launch_shard_merge(const RowParams* params, const RowState* state, uint32_t 
                        const q38s_candidate* gathered, uint32_t n_shards, uint32_t k_local,
                        q38s_decision_v1* decisions, void* stream) {
     if (rows == 0) return cudaSuccess;
-    uint32_t p2 = 1;
-    while (p2 < n_shards * k_local) p2 <<= 1;
-    const size_t smem = static_cast<size_t>(p2) * 32;
-    cudaError_t e = cudaFuncSetAttribute(shard_merge_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+    if (n_shards > kMaxShards) return cudaErrorInvalidValue;
+    const size_t smem = static_cast<size_t>(n_shards) * k_local * 8 + static_cast<size_t>(k_local) * 32;
+    static size_t configured[64] = {};  // largest shared-memory size set, per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (smem > 48 * 1024 && smem > configured[dev]) {
+        e = cudaFuncSetAttribute(shard_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        configured[dev] = smem;
+    }
     shard_merge_kernel<<<rows, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(
         params, state, gathered, rows, n_shards, k_local, decisions);
     return cudaGetLastError();

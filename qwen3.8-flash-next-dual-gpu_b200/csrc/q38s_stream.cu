@@ -1969,7 +1969,9 @@ __device__ __forceinline__ void finish_row(const SampleArgs& a, const Row& r, ui
         row_error(a, r, Q38S_ROW_NO_FINITE);
     } else if (flags & kFOverflow) {
         // the general path runs in general_kernel, launched behind this one
+        // (or by the caller, told through the row's status)
         if (threadIdx.x == 0) a.deferred[r.v] = 1u;
+        if (a.host_general) write_decision(a, r, -1, kRowDeferred);
         return;
     } else {
         double* w = reinterpret_cast<double*>(area);  // over the dead candidate buffer
@@ -2731,7 +2733,7 @@ static int launch_stream_t(const SampleArgs& a_in, void* stream) {
     if (a.segs == 1) {
         kern<<<grid, kBlock, smem, static_cast<cudaStream_t>(stream)>>>(a);
         e = cudaGetLastError();
-        return e != cudaSuccess ? e : launch_general<DT>(a, stream, sms[dev]);
+        return (e != cudaSuccess || a.host_general) ? e : launch_general<DT>(a, stream, sms[dev]);
     }
     // one cluster of segs CTAs per row: CTA rank = segment
     cudaLaunchConfig_t cfg = {};
@@ -2747,7 +2749,18 @@ static int launch_stream_t(const SampleArgs& a_in, void* stream) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, kern, a);
-    return e != cudaSuccess ? e : launch_general<DT>(a, stream, sms[dev]);
+    return (e != cudaSuccess || a.host_general) ? e : launch_general<DT>(a, stream, sms[dev]);
+}
+
+int launch_general_only(const SampleArgs& a, void* stream) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    return a.dtype == Q38S_DTYPE_BF16 ? launch_general<Q38S_DTYPE_BF16>(a, stream, sms)
+                                      : launch_general<Q38S_DTYPE_F32>(a, stream, sms);
 }
 
 int launch_stream(const SampleArgs& a, void* stream) {

@@ -20,8 +20,9 @@ Distributions:
         T ~ U[0.3, 1.2]; top_k = 0 with probability 1/4 else U{1..100};
         top_p ~ U[0.5, 1.0]; min_p ~ U[0, 0.1]; repetition ~ U[1.0, 1.2];
         history length U{1..32,768} uniform tokens.
-  cfg5  1,024 rows fp32 with the cfg4 row distribution; T 0.8, top_k 64 per
-        shard, top_p 0.9, repetition 1.1, 1,024-token history per row.
+  cfg5  1,024 rows fp32 with the cfg4 row distribution (cfg5_row: each row
+        from its own seed); T 0.8, top_k 64 per shard, top_p 0.9, repetition
+        1.1, 1,024-token history per row.
 """
 from __future__ import annotations
 
@@ -171,3 +172,13 @@ def cfg5_spec(seed: int = 5, rows: int = 1024, vocab: int = VOCAB, history: int 
 
 def cfg5_logits(seed: int = 5, rows: int = 1024, vocab: int = VOCAB, batch: int = 0):
     return cfg4_logits(batch=batch, seed=seed, rows=rows, vocab=vocab, dtype="f32")
+
+
+def cfg5_row(r: int, seed: int = 5, vocab: int = VOCAB) -> np.ndarray:
+    """Row r of the vocab-parallel benchmark, generated on its own (so a rank
+    can build its column shard and a checker any single row): fp32
+    N(0, 2.5^2) with the Zipf(1.1)-ranked spikes of the cfg4 distribution."""
+    rng = np.random.default_rng([seed, 0x55, r])
+    row = _gauss_row(rng, vocab, 2.5)
+    zipf_spikes(rng, row)
+    return row

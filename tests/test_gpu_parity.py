@@ -511,3 +511,34 @@ def test_cfg4_batch_matches_canonical_oracle(cuda):
         o = O.prepare_row(params[r], logits[r], counts[r], (), O.TIE_CANONICAL, cap=4096)
         assert is_boundary(o, configs[r].top_p), f"row {r}"
     print(f"cfg4: {len(bad)} boundary cases of {spec.rows}")
+
+
+def test_one_session_general_rows(cuda):
+    """The one-session sampler launches the general kernel itself when its
+    row is deferred (top_k = 0 at full vocabulary): decisions equal the
+    canonical oracle's over a few committed steps, for bf16 and fp32."""
+    import torch
+    rng = np.random.default_rng(808)
+    vocab = synth.VOCAB
+    for dtype in ("bf16", "f32"):
+        cfg = q38s.config_v2(top_k=0, top_p=0.9, temperature=1.0, repetition_penalty=1.1,
+                             seed=4242)
+        s = q38s.Sampler(vocab, cfg)
+        hist = rng.integers(0, vocab, 500).astype(np.int32)
+        s.commit_tokens(hist)
+        counts = np.bincount(hist, minlength=vocab).astype(np.uint32)
+        for step in range(4):
+            x = rng.normal(0, 2.5, vocab).astype(np.float32)
+            synth.zipf_spikes(rng, x)
+            logits = synth.f32_to_bf16_rne(x) if dtype == "bf16" else x
+            tok, rb, ra = s.prepare_device(to_torch(logits, cuda))
+            p = oracle_params(cfg, rb)
+            o = O.prepare_row(p, logits, counts, (), O.TIE_CANONICAL, cap=64)
+            if tok != o.token:
+                full = O.prepare_row(p, logits, counts, (), O.TIE_CANONICAL)
+                assert is_boundary(full, 0.9), f"{dtype} step {step}: {tok} vs {o.token}"
+            assert s.prepare_device(to_torch(logits, cuda)) == (tok, rb, ra)  # retry
+            s.commit((tok, rb, ra))
+            s.commit_token(tok)
+            counts[tok] += 1
+        torch.cuda.synchronize()
