@@ -21,13 +21,14 @@ data path (strong scaling: the headline value).  The line adds weak scaling
 of the candidates, merge and draw, with each phase's time).
 
 N = 1 adds configuration 2 (batch-1 latency), configuration 3 (speculative
-verification), configuration 4 over eight parameter draws, and the CPU
-baseline.
+verification), configuration 4 over eight parameter draws, greedy argmax and
+MoE router top-k device times, and the CPU baseline.
 
 --impl reference times the reference's own CPU implementation
 (src/sampling.cc compiled unmodified into oracle/_ref/libq38ref.so, one
 TransactionalSampler per row, rows spread over all host threads) on the same
-workload and metric.
+workload and metric; with a GPU present its line adds the device times of
+the reference's own argmax and router kernels at the same shapes.
 """
 from __future__ import annotations
 
@@ -403,6 +404,59 @@ def extra_single_gpu(args, dev, stream):
         out.update(batch1_latency(dev, stream))
     if "cfg3" in args.workloads:
         out.update(mtp_bench(dev, stream))
+    if "kernels" in args.workloads:
+        out["greedy_and_router"] = device_kernel_times("ours", dev, stream)
+    return out
+
+
+def device_kernel_times(impl, dev, stream, launches=500):
+    """Greedy argmax (one row of 151,936 and of 248,320 bf16 logits) and the
+    MoE router top-k (512 experts, top 10, normalised: 1 token, the decode
+    shape, and 64 tokens), mean device time per launch in µs from CUDA events
+    on the launch stream over `launches` back-to-back launches.  impl "ours"
+    calls q38s_argmax_bf16 / q38s_topk_router_bf16; "reference" the
+    reference's own cuda_argmax_bf16 / cuda_topk_router_bf16 (its
+    cuda/q38_kernels.cu compiled unmodified into oracle/_ref)."""
+    import torch
+    if impl == "ours":
+        import q38s
+        argmax = lambda x, o: q38s.argmax_bf16(x, o, stream=stream)  # noqa: E731
+        router = lambda w, i, p: q38s.topk_router_bf16(w, i, p, 10, True,  # noqa: E731
+                                                       stream=stream)
+    else:
+        import oracle as O
+        if not O.ref_kernels_available():
+            return {"unavailable": "oracle/_ref/libq38ref_kernels.so not built"}
+        argmax = lambda x, o: O.ref_argmax_bf16(x.data_ptr(), x.numel(),  # noqa: E731
+                                                o.data_ptr(), stream.cuda_stream, dev.index)
+        router = lambda w, i, p: O.ref_topk_router_bf16(  # noqa: E731
+            w.data_ptr(), i.data_ptr(), p.data_ptr(), w.shape[0], w.shape[1], 10, True,
+            stream.cuda_stream, dev.index)
+    rng = np.random.default_rng(77)
+
+    def timed(fn):
+        with torch.cuda.stream(stream):
+            for _ in range(20):
+                fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(launches):
+                fn()
+            e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / launches
+
+    out = {"unit": "us per launch", "launches": launches}
+    res = torch.zeros(1, dtype=torch.int32, device=dev)
+    for n in (151_936, 248_320):
+        x = bf16_tensor(synth.f32_to_bf16_rne(rng.normal(0, 2.5, n).astype(np.float32)), dev)
+        out[f"argmax_{n}"] = timed(lambda: argmax(x, res))
+    for tokens in (1, 64):
+        w = bf16_tensor(synth.f32_to_bf16_rne(
+            rng.normal(0, 1.5, (tokens, 512)).astype(np.float32)), dev)
+        ids = torch.zeros((tokens, 10), dtype=torch.int32, device=dev)
+        wts = torch.zeros((tokens, 10), dtype=torch.float32, device=dev)
+        out[f"router_{tokens}x512_top10"] = timed(lambda: router(w, ids, wts))
     return out
 
 
@@ -684,7 +738,7 @@ def run_reference(args, rank, world):
         O.ref_prepare_rows(sub_samplers, sub_logits, threads)
     dt = time.perf_counter() - t0
     value = len(sub) * args.steps / dt
-    return {"impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s",
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -697,6 +751,14 @@ def run_reference(args, rank, world):
                                        "sampling.cc prepare() on std::threads"},
             "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    if "kernels" in args.workloads:
+        import torch
+        if torch.cuda.is_available():
+            dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+            torch.cuda.set_device(dev)
+            line["greedy_and_router"] = device_kernel_times("reference", dev,
+                                                            torch.cuda.Stream(dev))
+    return line
 
 
 def main():
@@ -705,7 +767,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workloads", default="cfg4,cfg2,cfg3,cfg5,draws,cpu",
+    ap.add_argument("--workloads", default="cfg4,cfg2,cfg3,cfg5,draws,kernels,cpu",
                     help="comma list of the measurements to run (cfg4 always runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -300,6 +300,24 @@ int q38s_argmax_bf16(const uint16_t* logits, uint32_t count, int32_t* output,
                      void* stream, int device);
 
 /* ------------------------------------------------------------------------
+ * MoE router top-k: replaces cuda_topk_router_bf16 (cuda/q38_kernels.cu:
+ * 667-687, kernels :358-480) with the same arguments, checks and results.
+ * For each of `tokens` rows of `experts` bf16 logits (row-major, device):
+ * the top_k experts (top_k <= 32) and their weights, expert_ids[t * top_k +
+ * r] / expert_weights[t * top_k + r].  With 512 experts and normalisation
+ * (the reference's decode path, unless Q38_CUDA_DECODE_TOPK is "scalar",
+ * "0" or "false") experts are ordered by logit, lowest expert first on ties,
+ * and weight_r = expf(logit_r - logit_0) / sum of those over the ranks;
+ * otherwise by p = expf(logit - max) (lowest expert first on equal p) and
+ * weight_r = p_r / (normalize_top_k ? sum of the top_k p : sum of every p),
+ * the sums sequential in fp32 in the reference's order.  At most 3,072
+ * experts per token (the reference takes any count). */
+int q38s_topk_router_bf16(const uint16_t* logits, int32_t* expert_ids,
+                          float* expert_weights, uint32_t tokens,
+                          uint32_t experts, uint32_t top_k,
+                          int normalize_top_k, void* stream, int device);
+
+/* ------------------------------------------------------------------------
  * Failure injection, for tests of the bounded device waits only.  No
  * counterpart in the reference (its sampler runs on the host and has no
  * device waits).

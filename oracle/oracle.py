@@ -218,6 +218,50 @@ class RefSampler:
         self._lib.q38ref_reset(self._h)
 
 
+REF_KERNELS_LIB = os.path.join(HERE, "_ref", "libq38ref_kernels.so")
+_refk = None
+
+
+def ref_kernels_available() -> bool:
+    return os.path.exists(REF_KERNELS_LIB)
+
+
+def _load_ref_kernels():
+    """The reference's own device kernels (cuda/q38_kernels.cu, unmodified,
+    built for sm_100a): greedy argmax and the MoE router top-k."""
+    global _refk
+    if _refk is None:
+        lib = C.CDLL(REF_KERNELS_LIB)
+        lib.q38ref_argmax_bf16.argtypes = [_P, C.c_uint32, _P, _P, C.c_int, C.c_char_p,
+                                           C.c_size_t]
+        lib.q38ref_topk_router_bf16.argtypes = [_P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32,
+                                                C.c_int, _P, C.c_int, C.c_char_p, C.c_size_t]
+        _refk = lib
+    return _refk
+
+
+def ref_argmax_bf16(logits_ptr: int, count: int, out_ptr: int, stream_ptr: int, device: int):
+    """cuda_argmax_bf16 of the reference on device buffers (stream must be a
+    real stream, as the reference requires)."""
+    err = C.create_string_buffer(256)
+    rc = _load_ref_kernels().q38ref_argmax_bf16(logits_ptr, count, out_ptr, stream_ptr, device,
+                                                err, 256)
+    if rc:
+        raise SamplerError(rc, err.value.decode())
+
+
+def ref_topk_router_bf16(logits_ptr: int, ids_ptr: int, weights_ptr: int, tokens: int,
+                         experts: int, top_k: int, normalize: bool, stream_ptr: int,
+                         device: int):
+    """cuda_topk_router_bf16 of the reference on device buffers."""
+    err = C.create_string_buffer(256)
+    rc = _load_ref_kernels().q38ref_topk_router_bf16(logits_ptr, ids_ptr, weights_ptr, tokens,
+                                                     experts, top_k, int(normalize), stream_ptr,
+                                                     device, err, 256)
+    if rc:
+        raise SamplerError(rc, err.value.decode())
+
+
 def ref_prepare_rows(samplers: list[RefSampler], logits_bf16: np.ndarray, threads: int):
     """prepare() on one reference sampler per row, rows spread over threads."""
     lib = _load_ref()

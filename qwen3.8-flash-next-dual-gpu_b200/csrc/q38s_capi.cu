@@ -9,6 +9,7 @@
 #include <cmath>
 #include <cstdio>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -500,6 +501,31 @@ int q38s_shard_merge_sample(const q38s_batch* b, const q38s_candidate* gathered,
     const int e = launch_shard_merge(b->d_params, b->d_state, b->rows, gathered, n_shards,
                                      k_local, decisions, stream);
     if (e != cudaSuccess) return cuda_fail(static_cast<cudaError_t>(e), "shard_merge_sample");
+    return ok();
+}
+
+int q38s_topk_router_bf16(const uint16_t* logits, int32_t* expert_ids, float* expert_weights,
+                          uint32_t tokens, uint32_t experts, uint32_t top_k,
+                          int normalize_top_k, void* stream, int device) {
+    // q38_kernels.cu:671-673: the reference's argument checks and message
+    if (!logits || !expert_ids || !expert_weights || tokens == 0 || experts == 0 ||
+        top_k == 0 || top_k > experts || top_k > 32)
+        return fail(Q38S_INVALID_ARGUMENT, "invalid top-k router buffers");
+    if (experts > 3072)
+        return fail(Q38S_INVALID_ARGUMENT, "router experts above 3,072 per token");
+    if (device < 0) return fail(Q38S_INVALID_ARGUMENT, "invalid CUDA kernel launch context");
+    // the reference's dispatch (q38_kernels.cu:34-42, :674): its 512-expert
+    // decode path orders by logit, unless Q38_CUDA_DECODE_TOPK disables it
+    static const bool decode_path = [] {
+        const char* v = std::getenv("Q38_CUDA_DECODE_TOPK");
+        return !v || (std::strcmp(v, "scalar") != 0 && std::strcmp(v, "0") != 0 &&
+                      std::strcmp(v, "false") != 0);
+    }();
+    const int by_logit = (experts == 512 && normalize_top_k && decode_path) ? 1 : 0;
+    DeviceGuard g(device);
+    const int e = launch_topk_router(logits, expert_ids, expert_weights, tokens, experts, top_k,
+                                     normalize_top_k ? 1 : 0, by_logit, stream);
+    if (e != cudaSuccess) return cuda_fail(static_cast<cudaError_t>(e), "topk_router_bf16");
     return ok();
 }
 

@@ -137,5 +137,8 @@ int launch_shard_merge(const RowParams* params, const RowState* state, uint32_t 
                        uint32_t k_local, q38s_decision_v1* decisions, void* stream);
 int launch_argmax_bf16(const uint16_t* logits, uint32_t count, int32_t* out,
                        void* stream);
+int launch_topk_router(const uint16_t* logits, int32_t* expert_ids, float* expert_weights,
+                       uint32_t tokens, uint32_t experts, uint32_t top_k, int normalize,
+                       int by_logit, void* stream);
 
 }  // namespace q38s

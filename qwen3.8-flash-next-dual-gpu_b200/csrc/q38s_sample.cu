@@ -274,6 +274,91 @@ __global__ void __launch_bounds__(kThreads) shard_merge_kernel(
     }
 }
 
+// ------------------------------------------------------ MoE router
+// Router top-k (replaces the reference's cuda_topk_router_bf16,
+// q38_kernels.cu:667-687, kernels :358-480), one warp per token, the token's
+// logits in shared memory.  The top_k experts come from top_k rounds of a
+// warp-wide maximum of 64-bit keys (a selected key is cleared):
+//   by_logit  (512 experts, normalised; the reference's decode path): key
+//             (logit desc, expert asc); numerator expf(logit - largest);
+//   otherwise (the reference's general path): key (expf(x - max) desc,
+//             expert asc), max = fmaxf over the token's logits.
+// The denominators are the reference's sequential fp32 sums: over the ranks
+// (normalised) or over all experts in expert order; weight = numerator /
+// denominator.
+__global__ void __launch_bounds__(kThreads) topk_router_kernel(
+    const uint16_t* logits, int32_t* expert_ids, float* expert_weights, uint32_t tokens,
+    uint32_t experts, uint32_t top_k, int normalize, int by_logit) {
+    extern __shared__ __align__(16) unsigned char sm[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t token = blockIdx.x * (kThreads / 32) + warp;
+    if (token >= tokens) return;
+    float* x = reinterpret_cast<float*>(sm) + static_cast<size_t>(warp) * experts;
+    float* p = x + static_cast<size_t>(kThreads / 32) * experts;  // expf(x - max), general path
+    const uint16_t* row = logits + static_cast<size_t>(token) * experts;
+    float mx = -3.402823466e+38f;
+    for (uint32_t e = lane; e < experts; e += 32) {
+        const float v = __uint_as_float(static_cast<uint32_t>(row[e]) << 16);
+        x[e] = v;
+        mx = fmaxf(mx, v);
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (!by_logit)
+        for (uint32_t e = lane; e < experts; e += 32) p[e] = expf(x[e] - mx);
+    __syncwarp();
+    __shared__ float num[kThreads / 32][32];
+    __shared__ int32_t ids[kThreads / 32][32];
+    float top_logit = 0.0f;
+    for (uint32_t rank = 0; rank < top_k; ++rank) {
+        uint64_t best = 0;
+        for (uint32_t e = lane; e < experts; e += 32) {
+            const float f = by_logit ? x[e] : p[e];
+            const uint64_t key = (static_cast<uint64_t>(float_key(f)) << 32) | (0xffffffffu - e);
+            if (f == f && key > best) best = key;  // a selected entry holds NaN
+        }
+        best = warp_max_u64(best);
+        if (best == 0) {  // nothing left that is a number: the reference's empty slot
+            if (lane == 0) {
+                ids[warp][rank] = -1;
+                num[warp][rank] = -3.402823466e+38f;
+            }
+            __syncwarp();
+            continue;
+        }
+        const uint32_t e = rank_token(best);
+        if (lane == 0) {
+            ids[warp][rank] = static_cast<int32_t>(e);
+            num[warp][rank] = by_logit ? x[e] : p[e];
+        }
+        __syncwarp();
+        if (lane == (e & 31)) {  // the owner of expert e takes it out
+            if (by_logit) x[e] = __uint_as_float(0x7fffffffu);
+            else p[e] = __uint_as_float(0x7fffffffu);
+        }
+        __syncwarp();
+    }
+    if (lane == 0) {
+        if (by_logit) {
+            top_logit = num[warp][0];
+            for (uint32_t r = 0; r < top_k; ++r) num[warp][r] = expf(num[warp][r] - top_logit);
+        }
+        float den = 0.0f;
+        if (normalize) {
+            for (uint32_t r = 0; r < top_k; ++r) den += num[warp][r];
+        } else {
+            // the sum over all experts in expert order (selected entries were
+            // cleared: recompute them)
+            for (uint32_t e = 0; e < experts; ++e)
+                den += expf(__uint_as_float(static_cast<uint32_t>(row[e]) << 16) - mx);
+        }
+        for (uint32_t r = 0; r < top_k; ++r) {
+            const size_t o = static_cast<size_t>(token) * top_k + r;
+            expert_ids[o] = ids[warp][r];
+            expert_weights[o] = num[warp][r] / den;
+        }
+    }
+}
+
 // --------------------------------------------------------- argmax
 // Greedy selection (replaces argmax_bf16_kernel, q38_kernels.cu:320-356):
 // largest value above -3.402823466e38, lowest index among equals, -1 when
@@ -362,6 +447,28 @@ int launch_shard_merge(const RowParams* params, const RowState* state, uint32_t 
     }
     shard_merge_kernel<<<rows, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(
         params, state, gathered, rows, n_shards, k_local, decisions);
+    return cudaGetLastError();
+}
+
+int launch_topk_router(const uint16_t* logits, int32_t* expert_ids, float* expert_weights,
+                       uint32_t tokens, uint32_t experts, uint32_t top_k, int normalize,
+                       int by_logit, void* stream) {
+    constexpr uint32_t kWarps = kThreads / 32;
+    const size_t smem = static_cast<size_t>(2) * kWarps * experts * sizeof(float);
+    static size_t configured[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (smem > 48 * 1024 && smem > configured[dev]) {
+        e = cudaFuncSetAttribute(topk_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        configured[dev] = smem;
+    }
+    topk_router_kernel<<<(tokens + kWarps - 1) / kWarps, kThreads, smem,
+                         static_cast<cudaStream_t>(stream)>>>(
+        logits, expert_ids, expert_weights, tokens, experts, top_k, normalize, by_logit);
     return cudaGetLastError();
 }
 

@@ -39,7 +39,7 @@ EXPORTS = (
     "q38s_batch_reset", "q38s_batch_states", "q38s_batch_commit_tokens", "q38s_batch_prepare",
     "q38s_batch_commit", "q38s_batch_sample_commit",
     "q38s_mtp_verify", "q38s_shard_topk", "q38s_shard_merge_sample", "q38s_argmax_bf16",
-    "q38s_testing_set_fault", "q38s_prepare_noalloc",
+    "q38s_topk_router_bf16", "q38s_testing_set_fault", "q38s_prepare_noalloc",
 )
 
 
@@ -151,6 +151,7 @@ def lib():
         L.q38s_shard_merge_sample.argtypes = [P, P, u32, u32, P, P]
         L.q38s_argmax_bf16.argtypes = [P, u32, P, P, i32]
         L.q38s_testing_set_fault.argtypes = [u32, u64]
+        L.q38s_topk_router_bf16.argtypes = [P, P, P, u32, u32, u32, i32, P, i32]
         _lib = L
     return _lib
 
@@ -434,6 +435,16 @@ def make_distribution(rows: int, capacity: int, device):
                                  ("tokens", "values", "probs", "n_candidates", "n_retained",
                                   "total", "draw")))
     return s, t
+
+
+def topk_router_bf16(logits, expert_ids, expert_weights, top_k: int, normalize: bool = True,
+                     stream=None, device: int = 0):
+    """MoE router top-k over torch bf16 logits [tokens, experts] into int32
+    ids and float32 weights [tokens, top_k]."""
+    tokens, experts = logits.shape
+    _check(lib().q38s_topk_router_bf16(logits.data_ptr(), expert_ids.data_ptr(),
+                                       expert_weights.data_ptr(), tokens, experts, top_k,
+                                       int(normalize), _stream_ptr(stream), device))
 
 
 def argmax_bf16(logits, output, stream=None, device: int = 0):

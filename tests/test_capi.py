@@ -70,6 +70,9 @@ def test_host_validation_without_gpu():
     assert L.q38s_sampler_create_v2(0, 3, C.byref(v2), C.byref(h)) == q38s.INVALID_ARGUMENT
     assert L.q38s_argmax_bf16(None, 0, None, None, 0) == q38s.INVALID_ARGUMENT
     assert L.q38s_last_error().decode() == "invalid BF16 argmax buffers"
+    assert L.q38s_topk_router_bf16(None, None, None, 1, 512, 10, 1, None, 0) == \
+        q38s.INVALID_ARGUMENT
+    assert L.q38s_last_error().decode() == "invalid top-k router buffers"
     wide = q38s.config_v1(top_k=20)
     assert L.q38s_sampler_create(0, (1 << 20) + 1, C.byref(wide), C.byref(h)) == \
         q38s.INVALID_ARGUMENT
