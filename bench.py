@@ -673,6 +673,103 @@ def vocab_parallel(args, rank, world, dev, stream, dist):
                           "eagerly"}
 
 
+PROFILE_CASES = {
+    # case: (kernel the capture selects, what one launch covers)
+    "general": ("general_kernel", "4 rows x 151,936 bf16 (cfg4 distribution), top_k 0, "
+                "top_p 0.9, T 1.0, repetition 1.1, 2,000-token histories: every row "
+                "deferred to the general kernel"),
+    "cfg2": ("stream_kernel", "batch-1: 1 row x 151,936 bf16, cfg2 parameters, history "
+             "8,192, split over a cluster"),
+    "cfg3": ("stream_kernel", "MTP verification: 65 target + 64 draft rows x 151,936 fp32"),
+    "shard_topk": ("stream_kernel", "1,024 rows x 18,992 fp32 (one of 8 column shards of "
+                   "cfg5), local top-64"),
+    "shard_merge": ("shard_merge_kernel", "1,024 rows, 8 shards x 64 candidates, merge, "
+                    "top_p 0.9 draw"),
+    "argmax": ("argmax_bf16_kernel", "greedy argmax over 248,320 bf16 logits"),
+    "router": ("topk_router_kernel", "MoE router top-10 over 64 tokens x 512 experts"),
+}
+
+
+def profile_case(name, dev, stream, launches=4):
+    """A small run of one kernel for an ncu capture (`--profile CASE`): the
+    case's setup, then `launches` launches of the kernel on one GPU."""
+    import torch
+    import q38s
+    rng = np.random.default_rng(11)
+
+    def spiked(rows, cols):
+        x = rng.normal(0, 2.5, (rows, cols)).astype(np.float32)
+        for r in range(rows):
+            synth.zipf_spikes(rng, x[r])
+        return x
+
+    with torch.cuda.stream(stream):
+        if name == "general":
+            cfgs = [q38s.config_v2(top_k=0, top_p=0.9, repetition_penalty=1.1, seed=r + 1)
+                    for r in range(4)]
+            b = q38s.Batch(VOCAB, cfgs, device=dev.index)
+            b.commit_tokens([rng.integers(0, VOCAB, 2000).astype(np.int32) for _ in range(4)])
+            x = bf16_tensor(synth.f32_to_bf16_rne(spiked(4, VOCAB)), dev)
+            fn = lambda: b.prepare(x, stream=stream)  # noqa: E731
+        elif name == "cfg2":
+            c2 = synth.CFG2
+            cfg = q38s.config_v2(top_k=c2["top_k"], top_p=c2["top_p"], min_p=c2["min_p"],
+                                 temperature=c2["temperature"],
+                                 presence_penalty=c2["presence_penalty"], seed=c2["seed"])
+            b = q38s.Batch(VOCAB, [cfg], device=dev.index)
+            b.commit_tokens([synth.cfg2_history()])
+            x = bf16_tensor(synth.f32_to_bf16_rne(spiked(8, VOCAB)), dev)
+            dec = b.decisions_buffer()
+            it = iter(range(10 ** 9))
+            fn = lambda: b.sample_commit(x[next(it) % 8:][:1], dec, stream=stream)  # noqa
+        elif name == "cfg3":
+            c3 = synth.CFG3
+            b = q38s.Batch(VOCAB, [q38s.config_v2(top_k=c3["top_k"], top_p=c3["top_p"],
+                                                  temperature=c3["temperature"],
+                                                  seed=c3["seed"])], device=dev.index)
+            tgt, drf = synth.cfg3_rows(seed=3)
+            t_t, d_t = torch.from_numpy(tgt).to(dev), torch.from_numpy(drf).to(dev)
+            toks = torch.from_numpy(rng.integers(0, VOCAB, 64).astype(np.int32)).to(dev)
+            res = torch.zeros(q38s.C.sizeof(q38s.MtpResult), dtype=torch.uint8, device=dev)
+            fn = lambda: b.mtp_verify(0, t_t, d_t[:64], toks, result=res, stream=stream)  # noqa
+        elif name in ("shard_topk", "shard_merge"):
+            rows, k, world = 1024, 64, 8
+            w = VOCAB // world
+            spec = synth.cfg5_spec(rows=rows)
+            cfgs = [q38s.config_v2(top_k=64, top_p=0.9, temperature=0.8, repetition_penalty=1.1,
+                                   seed=int(spec.seed[r])) for r in range(rows)]
+            sb = q38s.Batch(VOCAB, cfgs, device=dev.index, shard=(0, w))
+            sb.commit_tokens([h[h < w] for h in spec.histories])
+            shard = torch.from_numpy(np.stack([synth.cfg5_row(r)[:w]
+                                               for r in range(rows)])).to(dev)
+            local = sb.shard_topk(shard, k, stream=stream)
+            if name == "shard_topk":
+                fn = lambda: sb.shard_topk(shard, k, out=local, stream=stream)  # noqa: E731
+            else:
+                gathered = local.repeat(world)
+                dec = sb.decisions_buffer()
+                fn = lambda: sb.shard_merge_sample(gathered, world, k, decisions=dec,  # noqa
+                                                   stream=stream)
+        elif name == "argmax":
+            x = bf16_tensor(synth.f32_to_bf16_rne(spiked(1, 248_320)[0]), dev)
+            out = torch.zeros(1, dtype=torch.int32, device=dev)
+            fn = lambda: q38s.argmax_bf16(x, out, stream=stream)  # noqa: E731
+        elif name == "router":
+            w = bf16_tensor(synth.f32_to_bf16_rne(
+                rng.normal(0, 1.5, (64, 512)).astype(np.float32)), dev)
+            ids = torch.zeros((64, 10), dtype=torch.int32, device=dev)
+            wts = torch.zeros((64, 10), dtype=torch.float32, device=dev)
+            fn = lambda: q38s.topk_router_bf16(w, ids, wts, 10, True, stream=stream)  # noqa
+        else:
+            raise SystemExit(f"unknown profile case {name}")
+        for _ in range(launches):
+            fn()
+    torch.cuda.synchronize()
+    kernel, what = PROFILE_CASES[name]
+    print(json.dumps({"profile_case": name, "kernel": kernel, "launches": launches,
+                      "workload": what}), flush=True)
+
+
 def cpu_baseline(spec, logits_bf16, budget_s: float = 12.0):
     """The reference's own sampler on the host cores over a bounded sample of
     the configuration-4 rows (one TransactionalSampler per row)."""
@@ -769,7 +866,15 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workloads", default="cfg4,cfg2,cfg3,cfg5,draws,kernels,cpu",
                     help="comma list of the measurements to run (cfg4 always runs)")
+    ap.add_argument("--profile", choices=sorted(PROFILE_CASES),
+                    help="run a small case of one kernel for an ncu capture and exit")
     args = ap.parse_args()
+    if args.profile:
+        import torch
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        profile_case(args.profile, dev, torch.cuda.Stream(dev))
+        return
     args.warmup = max(args.warmup, 3)
     args.workloads = set(args.workloads.split(","))
     world = int(os.environ.get("WORLD_SIZE", "1"))

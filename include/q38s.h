@@ -340,7 +340,7 @@ int q38s_testing_set_fault(uint32_t withhold_copies, uint64_t wait_cycles);
  * or a real-time loop in which an allocation (and the device-wide
  * synchronisation it can cause) is not allowed.  Every working buffer lives
  * in one fixed, statically sized device array inside this library
- * (4,588,288 bytes on every GPU that loads it, held until the process
+ * (4,982,016 bytes on every GPU that loads it, held until the process
  * exits); the caller passes only inputs and outputs.
  *
  * prepare() (sampling.cc:59-146 plus min_p) for `rows` rows of device logits

@@ -12,7 +12,8 @@ namespace q38s {
 constexpr int kThreads = 256;        // threads per CTA of the small kernels
 constexpr int kLeaderCap = 1024;     // candidates of a distribution / shard list
 constexpr uint32_t kMaxGeneralVocab = 1u << 20;  // column radix of the general path
-constexpr uint32_t kGAuxWords = 16384;           // general-path words after a row's keys
+constexpr uint32_t kGTeamWords = 24608;          // a deferred row's team words (barrier, slots)
+constexpr uint32_t kGAuxWords = 16384 + kGTeamWords;  // general-path words after a row's keys
 
 // 32-bit words of general-path scratch per virtual row (16-byte aligned rows).
 __host__ __device__ inline uint64_t scratch_stride(uint32_t vocab) {
@@ -81,7 +82,8 @@ struct SampleArgs {
     uint32_t k_out;
     // general-path scratch, scratch_stride 32-bit words per virtual row:
     // the exact key of every column (padded to a multiple of 4 words), then
-    // kGAuxWords of prefix sums and histograms
+    // kGAuxWords of histograms and, for a row shared by several CTAs, its
+    // team words
     uint32_t* scratch;
     uint64_t scratch_stride;
     // deferred[v] != 0: virtual row v takes the general path (general

@@ -362,24 +362,53 @@ __global__ void __launch_bounds__(kThreads) topk_router_kernel(
 // --------------------------------------------------------- argmax
 // Greedy selection (replaces argmax_bf16_kernel, q38_kernels.cu:320-356):
 // largest value above -3.402823466e38, lowest index among equals, -1 when
-// none.  One cluster of 8 CTAs x 512 threads; DSMEM reduction.
+// none.  One cluster of 8 CTAs x 512 threads: the row in 16-byte vectors
+// (four per thread in flight at once; scalar head and tail around them when
+// the row is not 16-byte aligned), 64-bit rank keys (value key, inverted
+// index) reduced by warp, CTA and DSMEM.
+__device__ __forceinline__ void argmax_take(unsigned long long& best, uint32_t bits, uint32_t i) {
+    const float v = __uint_as_float(bits << 16);
+    if (v > -3.402823466e+38f) {
+        const unsigned long long k = rank_key(float_key(v), i);
+        best = k > best ? k : best;
+    }
+}
 __global__ void __launch_bounds__(512) argmax_bf16_kernel(const uint16_t* logits,
                                                           uint32_t count, int32_t* out) {
     __shared__ unsigned long long red[16];
     __shared__ unsigned long long best_cta;
     cg::cluster_group cluster = cg::this_cluster();
-    const uint32_t S = cluster.num_blocks();
+    const uint32_t nt = cluster.num_blocks() * blockDim.x;
     const uint32_t me = cluster.block_rank();
-    const uint32_t per = (count + S - 1) / S;
-    const uint32_t lo = min(count, per * me), hi = min(count, lo + per);
+    const uint32_t gt = me * blockDim.x + threadIdx.x;
+    const uint32_t mis = static_cast<uint32_t>(reinterpret_cast<uintptr_t>(logits) & 15u) / 2u;
+    const uint32_t head = min(count, (8u - mis) & 7u);
+    const uint32_t nvec = (count - head) / 8u;
+    const uint4* vec = reinterpret_cast<const uint4*>(logits + head);
     unsigned long long best = 0;
-    for (uint32_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-        const float v = __uint_as_float(static_cast<uint32_t>(logits[i]) << 16);
-        if (v > -3.402823466e+38f) {
-            const unsigned long long k = rank_key(float_key(v), i);
-            best = k > best ? k : best;
+    for (uint32_t i = gt; i < head; i += nt) argmax_take(best, logits[i], i);
+    for (uint32_t base = 0; base < nvec; base += 4u * nt) {
+        uint4 w[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t j = base + k * nt + gt;
+            w[k] = j < nvec ? __ldg(&vec[j]) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t j = base + k * nt + gt;
+            if (j < nvec) {
+                const uint32_t i0 = head + j * 8u;
+                const uint32_t q[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    argmax_take(best, q[e] & 0xffffu, i0 + 2 * e);
+                    argmax_take(best, q[e] >> 16, i0 + 2 * e + 1);
+                }
+            }
         }
     }
+    for (uint32_t i = head + nvec * 8u + gt; i < count; i += nt) argmax_take(best, logits[i], i);
     best = warp_max_u64(best);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
     __syncthreads();
@@ -391,7 +420,7 @@ __global__ void __launch_bounds__(512) argmax_bf16_kernel(const uint16_t* logits
     cluster.sync();
     if (me == 0 && threadIdx.x == 0) {
         unsigned long long b = 0;
-        for (uint32_t s = 0; s < S; ++s) {
+        for (uint32_t s = 0; s < cluster.num_blocks(); ++s) {
             const unsigned long long o = *cluster.map_shared_rank(&best_cta, s);
             b = o > b ? o : b;
         }

@@ -1042,13 +1042,51 @@ constexpr uint32_t kGL = kGather;           // largest span gathered and sorted 
 constexpr uint32_t kAuxPm = kGB + 2;
 constexpr uint32_t kAuxSub = kAuxPm + 2 * (kGB + 1) + 1;
 constexpr uint32_t kEmitDepth = 3;
-static_assert(kAuxSub + kEmitDepth * kGB <= kGAuxWords, "general-path scratch words");
 static_assert(kGB * 12 <= kArea && kGL * 16 + (kGB + 1) * 4 <= kArea, "general-path area");
+
+// A deferred row is shared by a team of general-kernel CTAs when fewer rows
+// are deferred than the kernel has CTAs.  Member m takes the column chunk
+// [c0, c1) of every pass (32-column aligned), and each pass's reduction (a
+// maximum, a count, a histogram, the gathered members of a span) meets in
+// the row's team words in global memory: every member adds its CTA's
+// partial result with atomics, then the members wait for one another (a
+// GPU-scope barrier: an arrival counter and a generation word, bounded by
+// the wait limit) and read the total from L2.  The partial results of
+// phase q (q team barriers passed) go to slot q % 3; right after barrier q
+// the members zero slot (q + 1) % 3, one slice each (it was last read in
+// phase q - 1, and is next written in phase q + 1, after barrier q + 1).
+// The stream kernel zeroes the barrier words and slots 0 and 1 when it
+// defers the row.  A team of one CTA keeps every reduction in shared memory.
+constexpr uint32_t kSlotCnt = 0;             // [kGB] counts
+constexpr uint32_t kSlotMass = kGB;          // [kGB] 64-bit fixed-point masses
+constexpr uint32_t kSlotScal = 3 * kGB;      // [8] scalars: max, ~min, sum, gathered count
+constexpr uint32_t kSlotBuf = 3 * kGB + 8;   // [kGL] gathered rank keys
+constexpr uint32_t kSlotWords = kSlotBuf + 2 * kGL;
+constexpr uint32_t kTeamSync = 8;            // barrier words before slot 0
+constexpr uint32_t kTeamOff = 16384;         // team words: after the emission's words
+static_assert(kTeamSync + 3 * kSlotWords == kGTeamWords, "team words");
+static_assert(kTeamOff + kGTeamWords == kGAuxWords && kSlotWords % 4 == 0, "team layout");
+static_assert(kAuxSub + kEmitDepth * kGB <= kTeamOff, "emission words");
+
+// the general kernel's shared memory: the work area, the pass stages, the
+// level-1 prefix counts and masses
+constexpr uint32_t kPcBytes = ((kGB + 1) * 4 + 15) & ~15u;
+constexpr uint32_t kPcPmBytes = kPcBytes + (((kGB + 1) * 8 + 15) & ~15u);
+
+struct GTeam {             // in shared memory, one per CTA
+    uint32_t rank, size;   // this CTA's place in the row's team, and its members
+    uint32_t* sync;        // [0] arrivals, [1] generation
+    uint32_t* slots;       // three accumulation slots
+    uint32_t phase;        // team barriers passed
+    uint32_t failed;       // a barrier wait ran out: this CTA left the team
+};
 
 struct GRow {
     const uint32_t* keys;  // exact key per column (padded to whole 16-byte groups)
     uint4* stage;          // the passes' cp.async slots (kStageBytes of shared memory)
     Ctl* ctl;              // the CTA's control block
+    GTeam* t;              // the row's team
+    uint32_t c0, c1;       // this CTA's columns
     uint32_t V, tok0;
     float M;               // the row maximum
     uint32_t minp_key;     // smallest key whose weight reaches min_p (0: no min-p)
@@ -1173,27 +1211,156 @@ __device__ __forceinline__ void g_pass16(const unsigned char* src, uint64_t nbyt
     cp_async_wait<0>();
 }
 
-// Visits every column j < V with its key; f(col, key, valid) runs a
-// warp-uniform number of times.
+// Visits every column of this CTA's chunk with its key; f(col, key, valid)
+// runs a warp-uniform number of times.
 template <typename F>
 __device__ __forceinline__ void g_for_keys(const GRow g, F&& f) {
-    g_pass16(reinterpret_cast<const unsigned char*>(g.keys), static_cast<uint64_t>(g.V) * 4, g.stage,
-             *g.ctl, [&](uint32_t gi, const uint4& kv, bool) {
-                 const uint32_t c0 = gi * 4;
-                 f(c0, kv.x, c0 < g.V);
-                 f(c0 + 1, kv.y, c0 + 1 < g.V);
-                 f(c0 + 2, kv.z, c0 + 2 < g.V);
-                 f(c0 + 3, kv.w, c0 + 3 < g.V);
+    g_pass16(reinterpret_cast<const unsigned char*>(g.keys + g.c0),
+             static_cast<uint64_t>(g.c1 - g.c0) * 4, g.stage, *g.ctl,
+             [&](uint32_t gi, const uint4& kv, bool) {
+                 const uint32_t c0 = g.c0 + gi * 4;
+                 f(c0, kv.x, c0 < g.c1);
+                 f(c0 + 1, kv.y, c0 + 1 < g.c1);
+                 f(c0 + 2, kv.z, c0 + 2 < g.c1);
+                 f(c0 + 3, kv.w, c0 + 3 < g.c1);
              });
 }
 
-// P1: the exact key (sampling.cc:76-92) of every column into keys (16-byte
-// stores); the logits arrive through the pipelined pass when rows are
-// 16-byte aligned.  Returns the largest key.
+// ---- team reductions (no-ops for a team of one)
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// The slot this phase's partial results go to.
+__device__ __forceinline__ uint32_t* team_acc(const GTeam& t) {
+    return t.slots + (t.phase % 3u) * kSlotWords;
+}
+// Every member's partial results of the phase are in: the barrier, then the
+// zeroing of the slot after next.  Returns the slot that holds the totals,
+// or nullptr when this CTA has left the team (its wait ran out now or
+// before); a CTA that left neither adds nor waits any more, so the others'
+// next wait runs out as well and the row ends with a timeout status.
+__device__ __forceinline__ const uint32_t* team_sync(GTeam& t, Ctl& c) {
+    const uint32_t* done = team_acc(t);
+    cbar();  // the CTA's partial results are issued
+    if (threadIdx.x == 0) {
+        if (!t.failed) {
+            __threadfence();
+            const uint32_t gen = ld_acquire_gpu(t.sync + 1);
+            if (atom_add_acq_rel_gpu(t.sync, 1u) + 1u == t.size) {
+                t.sync[0] = 0;  // before the release: the next barrier counts from 0
+                st_release_gpu(t.sync + 1, gen + 1u);
+            } else {
+                const long long start = clock64();
+                while (ld_acquire_gpu(t.sync + 1) == gen) {
+                    if (clock64() - start > kWaitLimitCycles) {
+                        t.failed = 1u;
+                        break;
+                    }
+                }
+            }
+            __threadfence();
+        }
+        ++t.phase;
+    }
+    cbar();
+    if (t.failed) return nullptr;
+    uint4* z = reinterpret_cast<uint4*>(team_acc(t) + kSlotWords);  // slot (phase + 1) % 3
+    if (t.phase % 3u == 2u) z = reinterpret_cast<uint4*>(t.slots);
+    constexpr uint32_t n4 = kSlotWords / 4;
+    const uint32_t per = (n4 + t.size - 1) / t.size;
+    const uint32_t lo = min(n4, t.rank * per), hi = min(n4, lo + per);
+    for (uint32_t i = lo + threadIdx.x; i < hi; i += kCons) z[i] = make_uint4(0u, 0u, 0u, 0u);
+    return done;
+}
+// Team-wide maximum (and, with `lo`, minimum) of 32-bit values that the
+// CTA has reduced already; a CTA that left the team keeps its own.
+__device__ __forceinline__ uint32_t team_max(const GRow g, uint32_t v, uint32_t* lo, Ctl& c) {
+    GTeam& t = *g.t;
+    if (t.size == 1) return v;
+    uint32_t* acc = team_acc(t);
+    if (threadIdx.x == 0 && !t.failed) {
+        atomicMax(&acc[kSlotScal], v);
+        if (lo) atomicMax(&acc[kSlotScal + 1], ~*lo);
+    }
+    const uint32_t* tot = team_sync(t, c);
+    if (!tot) return v;
+    if (lo) *lo = ~__ldcg(&tot[kSlotScal + 1]);
+    return __ldcg(&tot[kSlotScal]);
+}
+__device__ __forceinline__ uint32_t team_sum(const GRow g, uint32_t v, Ctl& c) {
+    GTeam& t = *g.t;
+    if (t.size == 1) return v;
+    uint32_t* acc = team_acc(t);
+    if (threadIdx.x == 0 && !t.failed) atomicAdd(&acc[kSlotScal + 2], v);
+    const uint32_t* tot = team_sync(t, c);
+    return tot ? __ldcg(&tot[kSlotScal + 2]) : v;
+}
+// A shared-memory histogram of nb bins (counts hc, and with hm the split
+// 64-bit masses) replaced by the team's total.
+__device__ __forceinline__ void team_hist(const GRow g, uint32_t* hc, uint32_t* hm, uint32_t nb,
+                                          Ctl& c) {
+    GTeam& t = *g.t;
+    if (t.size == 1) return;
+    uint32_t* acc = team_acc(t);
+    cbar();  // the CTA's histogram is complete
+    if (!t.failed) {
+        for (uint32_t b = threadIdx.x; b < nb; b += kCons) {
+            if (hc[b]) atomicAdd(&acc[kSlotCnt + b], hc[b]);
+            if (hm) {
+                const unsigned long long m = get_u64_split(&hm[2 * b]);
+                if (m)
+                    atomicAdd(reinterpret_cast<unsigned long long*>(&acc[kSlotMass + 2 * b]), m);
+            }
+        }
+    }
+    const uint32_t* tot = team_sync(t, c);
+    if (!tot) return;
+    for (uint32_t b = threadIdx.x; b < nb; b += kCons) {
+        hc[b] = __ldcg(&tot[kSlotCnt + b]);
+        if (hm) {
+            hm[2 * b] = __ldcg(&tot[kSlotMass + 2 * b]);
+            hm[2 * b + 1] = __ldcg(&tot[kSlotMass + 2 * b + 1]);
+        }
+    }
+    cbar();
+}
+// The rank keys gathered in buf (n of them, n <= kGL in all) replaced by the
+// team's; returns their number.  Their order differs between runs: callers
+// sort them.
+__device__ __forceinline__ uint32_t team_gather(const GRow g, uint64_t* buf, uint32_t n, Ctl& c) {
+    GTeam& t = *g.t;
+    if (t.size == 1) return n;
+    uint32_t* acc = team_acc(t);
+    cbar();  // buf is complete (and n read by every thread)
+    if (threadIdx.x == 0)
+        c.bc_u32[1] = (t.failed || n == 0) ? 0u : atomicAdd(&acc[kSlotScal + 3], n);
+    cbar();
+    const uint32_t at = c.bc_u32[1];
+    uint64_t* gb = reinterpret_cast<uint64_t*>(acc + kSlotBuf);
+    if (!t.failed)
+        for (uint32_t i = threadIdx.x; i < n; i += kCons)
+            if (at + i < kGL) gb[at + i] = buf[i];
+    const uint32_t* tot = team_sync(t, c);
+    if (!tot) return n;
+    const uint32_t m = min(__ldcg(&tot[kSlotScal + 3]), kGL);
+    const uint64_t* src = reinterpret_cast<const uint64_t*>(tot + kSlotBuf);
+    for (uint32_t i = threadIdx.x; i < m; i += kCons) buf[i] = __ldcg(&src[i]);
+    cbar();
+    return m;
+}
+
+// P1: the exact key (sampling.cc:76-92) of every column of [c0, c1) into
+// keys (16-byte stores); the logits arrive through the pipelined pass when
+// rows are 16-byte aligned.  Returns the CTA's largest key.
 template <int DT>
 __device__ __forceinline__ uint32_t g_keys(const SampleArgs& a, const Row& r, const unsigned char* row,
                                            const uint32_t* pbm, uint32_t* keys, uint32_t V,
-                                           uint4* stage, Ctl& c) {
+                                           uint32_t c0, uint32_t c1, uint4* stage, Ctl& c) {
     constexpr uint32_t es = DT == Q38S_DTYPE_BF16 ? 2u : 4u;
     constexpr uint32_t pv = 16u / es;
     uint32_t kmax = 0;
@@ -1245,13 +1412,15 @@ __device__ __forceinline__ uint32_t g_keys(const SampleArgs& a, const Row& r, co
                 if (col0 + e < V) keys[col0 + e] = k[e];
         }
     };
+    const uint32_t q0 = c0 / pv;  // c0 is a multiple of 32
     if (a.use_tma) {
-        g_pass16(row, static_cast<uint64_t>(V) * es, stage, c, [&](uint32_t q, const uint4& w, bool valid) {
-            if (valid) group(q, w);
-        });
+        g_pass16(row + static_cast<size_t>(c0) * es, static_cast<uint64_t>(c1 - c0) * es, stage, c,
+                 [&](uint32_t q, const uint4& w, bool valid) {
+                     if (valid) group(q0 + q, w);
+                 });
     } else {
-        const uint32_t nvec = (V + pv - 1) / pv;
-        for (uint32_t q = threadIdx.x; q < nvec; q += kCons)
+        const uint32_t nvec = (c1 + pv - 1) / pv;
+        for (uint32_t q = q0 + threadIdx.x; q < nvec; q += kCons)
             group(q, load_vec<DT>(a, row, q * pv, min(pv, V - q * pv)));
     }
     return cmax_u32(kmax, c);  // its barriers also publish keys[] to the CTA
@@ -1279,6 +1448,7 @@ __device__ __forceinline__ uint32_t g_level1(const GRow g, bool weighted, unsign
         if (weighted) add_u64_split(&hm[2 * b], g_tw(d, b));
     });
     cbar();
+    team_hist(g, hc, weighted ? hm : nullptr, kGB, c);
     constexpr uint32_t kPer = kGB / kCons;
     uint32_t lc[kPer], sc = 0;
     double lm[kPer], sm = 0.0;
@@ -1344,8 +1514,10 @@ __device__ __forceinline__ void g_minmax(const GRow g, GSpan& s, Ctl& c) {
             hi = max(hi, key);
         }
     });
-    s.lo = cmin_u32(lo, c);
-    s.hi = cmax_u32(hi, c);
+    lo = cmin_u32(lo, c);
+    hi = cmax_u32(hi, c);
+    s.hi = team_max(g, hi, &lo, c);
+    s.lo = lo;
 }
 
 // The span's members as rank keys, sorted descending into `sorted`
@@ -1365,7 +1537,7 @@ __device__ __forceinline__ uint32_t g_gather_sorted(const GRow g, const GSpan s,
         warp_push(in, rank_key(key, g.tok0 + col), buf, kGL, &c.bc_u32[2]);
     });
     cbar();
-    const uint32_t n = min(c.bc_u32[2], kGL);
+    const uint32_t n = team_gather(g, buf, min(c.bc_u32[2], kGL), c);
     sort_desc(buf, n, sorted);
     return n;
 }
@@ -1444,6 +1616,7 @@ __device__ __forceinline__ uint32_t g_tie_col(const GRow g, uint32_t key, uint32
                 atomicAdd(&h[level == 0 ? (col >> 9) : (col & 511u)], 1u);
         });
         cbar();
+        team_hist(g, h, nullptr, nb, c);
         if (threadIdx.x == 0) {
             uint32_t left = need, d = 0;
             for (; d < nb - 1; ++d) {
@@ -1493,16 +1666,16 @@ __device__ __forceinline__ GLoc g_locate(const GRow g, const uint32_t* pc, const
 #pragma unroll
     for (uint32_t j = 0; j < kPer; ++j) {
         const uint32_t b = threadIdx.x * kPer + j;
-        const bool hit = mass ? (strict ? __ldcg(&pm[b + 1]) > tau : __ldcg(&pm[b + 1]) >= tau)
-                              : static_cast<double>(__ldcg(&pc[b + 1])) >= tau;
-        if (hit && first == 0xffffffffu && __ldcg(&pc[b + 1]) > __ldcg(&pc[b])) first = b;
+        const bool hit = mass ? (strict ? pm[b + 1] > tau : pm[b + 1] >= tau)
+                              : static_cast<double>(pc[b + 1]) >= tau;
+        if (hit && first == 0xffffffffu && pc[b + 1] > pc[b]) first = b;
     }
     first = cmin_u32(first, c);
     if (first == 0xffffffffu) {  // rounding: the target lies past the last bin
         uint32_t last = 0;
         for (uint32_t j = 0; j < kPer; ++j) {
             const uint32_t b = threadIdx.x * kPer + j;
-            if (__ldcg(&pc[b + 1]) > __ldcg(&pc[b])) last = b + 1;
+            if (pc[b + 1] > pc[b]) last = b + 1;
         }
         last = cmax_u32(last, c);
         if (last == 0) return GLoc{false, 0, 0, 0, 0.0};
@@ -1512,9 +1685,9 @@ __device__ __forceinline__ GLoc g_locate(const GRow g, const uint32_t* pc, const
     s.b1 = first;
     s.lo = 0;
     s.hi = 0xffffffffu;
-    s.above_cnt = __ldcg(&pc[first]);
-    s.above_mass = mass ? __ldcg(&pm[first]) : 0.0;
-    s.n = __ldcg(&pc[first + 1]) - s.above_cnt;
+    s.above_cnt = pc[first];
+    s.above_mass = mass ? pm[first] : 0.0;
+    s.n = pc[first + 1] - s.above_cnt;
     const double scale = g_bin_scale(first);
     bool bounded = false;
     for (int level = 0; level < 6; ++level) {
@@ -1548,6 +1721,7 @@ __device__ __forceinline__ GLoc g_locate(const GRow g, const uint32_t* pc, const
             }
         });
         cbar();
+        team_hist(g, hc, mass ? hm : nullptr, kGB, c);
         uint32_t lc[kPer], sc = 0;
         double lm[kPer], sm = 0.0;
 #pragma unroll
@@ -1771,7 +1945,7 @@ __device__ __forceinline__ void g_emit(const GRow g, const GOut o, const uint32_
     uint64_t* lk = reinterpret_cast<uint64_t*>(area + kGL * 8);
     uint32_t* bcnt = reinterpret_cast<uint32_t*>(area + kGL * 16);  // level-1 counts
     cbar();
-    for (uint32_t b = threadIdx.x; b < kGB; b += kCons) bcnt[b] = __ldcg(&pc[b + 1]) - __ldcg(&pc[b]);
+    for (uint32_t b = threadIdx.x; b < kGB; b += kCons) bcnt[b] = pc[b + 1] - pc[b];
     cbar();
     uint32_t pos = 0, b = 0;
     while (b < kGB && pos < o.n_emit) {
@@ -1792,8 +1966,7 @@ __device__ __forceinline__ void g_emit(const GRow g, const GOut o, const uint32_
             g_emit_big(g, o, s, pos, subh, area, c);
             // the level-1 counts live beside the sub-bin counts: reload them
             cbar();
-            for (uint32_t i = threadIdx.x; i < kGB; i += kCons)
-                bcnt[i] = __ldcg(&pc[i + 1]) - __ldcg(&pc[i]);
+            for (uint32_t i = threadIdx.x; i < kGB; i += kCons) bcnt[i] = pc[i + 1] - pc[i];
             cbar();
             pos += cnt;
             ++b;
@@ -1808,17 +1981,24 @@ __device__ __forceinline__ void g_emit(const GRow g, const GOut o, const uint32_
     }
 }
 
+// One deferred row by this CTA's part of its team; the leader (rank 0)
+// writes every output.  pcpm: shared memory for the level-1 prefix counts
+// (kGB + 1) and masses (kGB + 1 doubles).
 template <int DT>
 __device__ __forceinline__ void general_row(const SampleArgs& a, const Row& r, unsigned char* area,
-                                            uint4* stage, Ctl& c) {
+                                            uint4* stage, unsigned char* pcpm, GTeam& t, Ctl& c) {
     const uint32_t V = a.vocab;
     const uint32_t tok0 = a.col_begin;
+    const bool lead = t.rank == 0;
     uint32_t* keys = a.scratch + static_cast<size_t>(r.v) * a.scratch_stride;
     uint32_t* aux = keys + ((V + 3u) & ~3u);
-    uint32_t* pc = aux;
-    double* pm = reinterpret_cast<double*>(aux + kAuxPm);
     uint32_t* subh = aux + kAuxSub;
+    uint32_t* pc = reinterpret_cast<uint32_t*>(pcpm);
+    double* pm = reinterpret_cast<double*>(pcpm + kPcBytes);
     const unsigned char* row = row_ptr<DT>(a, r.v);
+    // this CTA's columns: 32-aligned chunks, one per member
+    const uint32_t chunk = ((V + t.size - 1) / t.size + 31u) & ~31u;
+    const uint32_t c0 = min(V, t.rank * chunk), c1 = min(V, c0 + chunk);
     // this call's penalised columns (bitmap plus additional tokens) in
     // shared memory when they fit
     const uint32_t words = (V + 31) / 32;
@@ -1826,11 +2006,11 @@ __device__ __forceinline__ void general_row(const SampleArgs& a, const Row& r, u
     if (r.pen && words * 4 <= kArea) {
         uint32_t* sbm = reinterpret_cast<uint32_t*>(area);
         cbar();
-        for (uint32_t i = threadIdx.x; i < words; i += kCons) sbm[i] = r.gbm[i];
+        for (uint32_t i = c0 / 32 + threadIdx.x; i < (c1 + 31) / 32; i += kCons) sbm[i] = r.gbm[i];
         cbar();
         for (uint32_t e = threadIdx.x; e < r.n_extra; e += kCons) {
             const uint32_t col = static_cast<uint32_t>(r.extra[e]) - tok0;
-            if (col < V) atomicOr(&sbm[col >> 5], 1u << (col & 31));
+            if (col >= c0 && col < c1) atomicOr(&sbm[col >> 5], 1u << (col & 31));
         }
         cbar();
         pbm = sbm;
@@ -1839,17 +2019,24 @@ __device__ __forceinline__ void general_row(const SampleArgs& a, const Row& r, u
     g.keys = keys;
     g.stage = stage;
     g.ctl = &c;
+    g.t = &t;
+    g.c0 = c0;
+    g.c1 = c1;
     g.V = V;
     g.tok0 = tok0;
-    const uint32_t M_key = g_keys<DT>(a, r, row, pbm, keys, V, g.stage, c);
+    const uint32_t M_key =
+        team_max(g, g_keys<DT>(a, r, row, pbm, keys, V, c0, c1, g.stage, c), nullptr, c);
     Q38S_TT(r.v, 6);
     g.M = key_float(M_key);
     g.minp_key = 0;
     g.has_cut = false;
     g.cut_key = 0;
     g.cut_col = 0;
+    auto fail = [&](int32_t status) {
+        if (lead) row_error(a, r, t.failed ? Q38S_ROW_TIMEOUT : status);
+    };
     if (a.mode != kModeShardTopK && (M_key <= kNegInfKey || isinf(g.M))) {
-        row_error(a, r, Q38S_ROW_NO_FINITE);
+        fail(Q38S_ROW_NO_FINITE);
         return;
     }
     // smallest key whose weight reaches min_p
@@ -1874,7 +2061,7 @@ __device__ __forceinline__ void general_row(const SampleArgs& a, const Row& r, u
         g_for_keys(g, [&](uint32_t, uint32_t key, bool valid) {
             cnt += valid && key >= g.minp_key;
         });
-        n0 = csum_u32(cnt, c);
+        n0 = team_sum(g, csum_u32(cnt, c), c);
         if (r.k_eff && r.k_eff < n0) {
             double unused;
             g_level1(g, false, area, pc, pm, &unused, c);
@@ -1895,6 +2082,11 @@ __device__ __forceinline__ void general_row(const SampleArgs& a, const Row& r, u
         s.lo = 0;
         s.hi = 0xffffffffu;
         const uint32_t m = g_gather_sorted(g, s, 0, kGB - 1, buf, lk, c);
+        if (!lead) return;
+        if (t.failed) {
+            fail(Q38S_ROW_TIMEOUT);
+            return;
+        }
         double* w = reinterpret_cast<double*>(area);  // over the dead gather buffer
         double* S = reinterpret_cast<double*>(area + kGL * 16);
         double* q = reinterpret_cast<double*>(area + kGL * 24);
@@ -1902,14 +2094,14 @@ __device__ __forceinline__ void general_row(const SampleArgs& a, const Row& r, u
         return;
     }
     if (a.mode == kModeShardTopK) {  // candidate lists hold at most kLeaderCap
-        row_error(a, r, Q38S_ROW_NORMALIZATION);
+        fail(Q38S_ROW_NORMALIZATION);
         return;
     }
     double Z = 0.0;
     g_level1(g, true, area, pc, pm, &Z, c);
     Q38S_TT(r.v, 13);
     if (!(Z > 0.0) || !isfinite(Z)) {
-        row_error(a, r, Q38S_ROW_NORMALIZATION);
+        fail(Q38S_ROW_NORMALIZATION);
         return;
     }
     uint32_t r_cnt = n0;
@@ -1932,8 +2124,9 @@ __device__ __forceinline__ void general_row(const SampleArgs& a, const Row& r, u
                         : g_locate(g, pc, pm, false, static_cast<double>(r_cnt), false, area, c);
     }
     Q38S_TT(r.v, 15);
-    if (!sel.found) {
-        row_error(a, r, Q38S_ROW_NORMALIZATION);
+    if (!lead) return;
+    if (!sel.found || t.failed) {
+        fail(Q38S_ROW_NORMALIZATION);
         return;
     }
     write_decision(a, r, static_cast<int32_t>(tok0 + sel.col), Q38S_ROW_OK);
@@ -1945,6 +2138,13 @@ __device__ __forceinline__ void general_row(const SampleArgs& a, const Row& r, u
             if (a.dist.draw) a.dist.draw[r.v] = draw;
         }
         if (a.dist.tokens || a.dist.values || a.dist.probs) {
+            // the leader alone, over the whole row (every member's keys are
+            // visible after the team's barriers)
+            cbar();
+            if (threadIdx.x == 0) t.size = 1;
+            cbar();
+            g.c0 = 0;
+            g.c1 = V;
             GOut o;
             o.tokens = a.dist.tokens;
             o.values = a.dist.values;
@@ -1969,7 +2169,13 @@ __device__ __forceinline__ void finish_row(const SampleArgs& a, const Row& r, ui
         row_error(a, r, Q38S_ROW_NO_FINITE);
     } else if (flags & kFOverflow) {
         // the general path runs in general_kernel, launched behind this one
-        // (or by the caller, told through the row's status)
+        // (or by the caller, told through the row's status); the row's team
+        // words start from zero
+        uint4* tw = reinterpret_cast<uint4*>(a.scratch + static_cast<size_t>(r.v) * a.scratch_stride +
+                                             ((a.vocab + 3u) & ~3u) + kTeamOff);
+        for (uint32_t i = threadIdx.x; i < (kTeamSync + 2 * kSlotWords) / 4; i += kCons)
+            tw[i] = make_uint4(0u, 0u, 0u, 0u);
+        cbar();
         if (threadIdx.x == 0) a.deferred[r.v] = 1u;
         if (a.host_general) write_decision(a, r, -1, kRowDeferred);
         return;
@@ -1981,40 +2187,77 @@ __device__ __forceinline__ void finish_row(const SampleArgs& a, const Row& r, ui
 }
 
 // ------------------------------------------------------------ general kernel
-// The rows the stream kernel deferred (deferred[v] != 0), one CTA per row at
-// a time; row v belongs to CTA v % gridDim.x.  Launched right behind the
-// stream kernel as its programmatic dependent: it may be scheduled early and
-// waits (griddepcontrol.wait) until the stream kernel has completed.  Each
-// CTA reads its rows' flags in one load per thread and clears the flags it
-// takes, so the flags are zero between launches; with no deferred row it
-// returns at once.  The stream kernel stays free of the general path's code.
+// The rows the stream kernel deferred (deferred[v] != 0; the stream kernel
+// writes every row's flag), launched right behind the stream kernel as its
+// programmatic dependent: it may be scheduled early and waits
+// (griddepcontrol.wait) until the stream kernel has completed.  Every CTA
+// reads all flags.  With D deferred rows and G CTAs: D >= G, CTA i takes the
+// deferred rows of rank i, i + G, ... alone; D < G, the CTAs form D teams of
+// G / D (team j takes the deferred row of rank j; CTAs past D * (G / D) have
+// nothing to do).  With no deferred row every CTA returns at once.  The
+// stream kernel stays free of the general path's code.
 template <int DT>
 __global__ void __launch_bounds__(kCons, 1) general_kernel(const SampleArgs a) {
     extern __shared__ __align__(1024) unsigned char gsm[];
     __shared__ Ctl c;
     __shared__ Row rs;
+    __shared__ GTeam gt;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     unsigned char* area = gsm;
     uint4* stage = reinterpret_cast<uint4*>(gsm + kArea);
-    for (uint32_t base = blockIdx.x; base < a.vrows; base += gridDim.x * kCons) {
-        const uint32_t v = base + threadIdx.x * gridDim.x;
-        const uint32_t mine = v < a.vrows && a.deferred[v] != 0 ? 1u : 0u;
+    unsigned char* pcpm = gsm + kArea + kStageBytes;
+    // D: the deferred rows
+    uint32_t D = 0;
+    for (uint32_t base = 0; base < a.vrows; base += kCons) {
+        const uint32_t v = base + threadIdx.x;
+        D += csum_u32(v < a.vrows && __ldcg(&a.deferred[v]) != 0 ? 1u : 0u, c);
+    }
+    if (D == 0) return;
+    const uint32_t G = gridDim.x;
+    const uint32_t T = D >= G ? 1u : G / D;     // team size
+    const uint32_t team = blockIdx.x / T;       // D >= G: the CTA's first rank
+    if (team >= D) return;
+    // the deferred rows in rank order, chunk by chunk; this CTA takes ranks
+    // team, team + G, ... (T == 1) or rank team alone (T > 1)
+    __shared__ uint32_t taken_rows[kCons];
+    uint32_t seen = 0;
+    for (uint32_t base = 0; base < a.vrows; base += kCons) {
+        const uint32_t v = base + threadIdx.x;
+        const uint32_t mine = v < a.vrows && __ldcg(&a.deferred[v]) != 0 ? 1u : 0u;
         uint32_t n;
-        const uint32_t pos = cscan_excl(mine, &n, c);  // the flagged rows, in order
-        if (mine) c.tkey[pos] = v;
+        const uint32_t pos = seen + cscan_excl(mine, &n, c);
+        // the first rank this CTA takes at or after `seen`
+        uint32_t first = 0xffffffffu;
+        if (team >= seen) first = team;
+        else if (T == 1) first = team + ((seen - team + G - 1) / G) * G;
+        uint32_t taken = 0;
+        if (first < seen + n) taken = T == 1 ? (seen + n - 1 - first) / G + 1 : 1u;
+        if (mine && pos >= first && pos < seen + n) {
+            if (T == 1 && (pos - first) % G == 0) taken_rows[(pos - first) / G] = v;
+            if (T > 1 && pos == first) taken_rows[0] = v;
+        }
         cbar();
-        for (uint32_t i = 0; i < n; ++i) {
-            const uint32_t vr = c.tkey[i];
+        for (uint32_t i = 0; i < taken; ++i) {
+            const uint32_t vr = taken_rows[i];
             cbar();
             if (threadIdx.x == 0) {
-                a.deferred[vr] = 0;
                 load_row(a, vr, rs);
+                gt.rank = T == 1 ? 0u : blockIdx.x % T;
+                gt.size = T;
+                uint32_t* aux = a.scratch + static_cast<size_t>(vr) * a.scratch_stride +
+                                ((a.vocab + 3u) & ~3u);
+                gt.sync = aux + kTeamOff;
+                gt.slots = aux + kTeamOff + kTeamSync;
+                gt.phase = 0;
+                gt.failed = 0;
             }
             cbar();
-            general_row<DT>(a, rs, area, stage, c);
-            row_done(a, area, c);
+            general_row<DT>(a, rs, area, stage, pcpm, gt, c);
+            if (gt.rank == 0) row_done(a, area, c);
             cbar();
         }
+        seen += n;
+        cbar();  // taken_rows is rewritten by the next chunk
     }
 }
 
@@ -2166,7 +2409,10 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
         // one copy of the row context per CTA, in shared memory: it is
         // needed in the row's tail, and registers are scarce in the stream
         // loop (every consumer finished the previous unit at its last barrier)
-        if (tid == 0) load_row(a, v, rs);
+        if (tid == 0) {
+            load_row(a, v, rs);
+            if (seg == 0) a.deferred[v] = 0u;  // set again if the row is deferred
+        }
         cbar();
         const Row& r = rs;
         Q38S_TT(u, 1);
@@ -2677,17 +2923,19 @@ static cudaError_t launch_general(const SampleArgs& a, void* stream, int sms) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    constexpr uint32_t smem = kArea + kStageBytes + kPcPmBytes;
     if (!configured[dev]) {
         e = cudaFuncSetAttribute(general_kernel<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(kArea + kStageBytes));
+                                 static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    const uint32_t grid = a.vrows < static_cast<uint32_t>(sms) ? a.vrows : static_cast<uint32_t>(sms);
+    // one CTA per SM (its shared memory admits no second): every CTA of a
+    // team is resident once the stream kernel has left the SMs
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
+    cfg.gridDim = dim3(static_cast<uint32_t>(sms));
     cfg.blockDim = dim3(kCons);
-    cfg.dynamicSmemBytes = kArea + kStageBytes;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

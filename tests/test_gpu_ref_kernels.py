@@ -149,6 +149,29 @@ def test_argmax_bit_exact_against_the_reference_kernel(cuda):
         assert a == b, f"n={x.size}: {a} vs reference {b}"
 
 
+def test_argmax_unaligned_rows_against_the_reference_kernel(cuda):
+    """Rows starting 1..7 elements past a 16-byte boundary (scalar head and
+    tail around the vector loads)."""
+    import torch
+    _need_ref()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(dev)
+    rng = np.random.default_rng(53)
+    x = (np.round(rng.normal(0, 2, 70_000) * 2) / 2).astype(np.float32)
+    d = torch.from_numpy(synth.f32_to_bf16_rne(x).view(np.int16)).to(dev)
+    for off in range(8):
+        for n in (1, 5, 9, 17, 4097, 65_000):
+            sl = d[off:off + n]
+            out = torch.full((2,), -7, dtype=torch.int32, device=dev)
+            torch.cuda.synchronize()
+            with torch.cuda.stream(stream):
+                q38s.argmax_bf16(sl, out[0:1], stream=stream)
+            O.ref_argmax_bf16(sl.data_ptr(), n, out[1:2].data_ptr(), stream.cuda_stream, 0)
+            stream.synchronize()
+            a, b = out.cpu().numpy()
+            assert a == b, f"offset {off}, n={n}: {a} vs reference {b}"
+
+
 def test_router_and_argmax_timed_against_the_reference(cuda):
     """Device time of both implementations at the reference's decode shapes
     (CUDA events on one stream, 200 launches each), printed; the argmax must
