@@ -210,6 +210,29 @@ __device__ uint32_t cscan_excl(uint32_t v, uint32_t* total, Ctl& c) {
     return before + inc - v;
 }
 
+// Exclusive prefix sum of doubles over the consumers in thread order.
+__device__ __forceinline__ double cscan_excl_f64(double v, double* total, Ctl& c) {
+    const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    double inc = v;
+    for (int o = 1; o < 32; o <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= static_cast<uint32_t>(o)) inc += y;
+    }
+    double excl = __shfl_up_sync(0xffffffffu, inc, 1);
+    if (lane == 0) excl = 0.0;
+    cbar();
+    if (lane == 31) c.red_u64[w] = static_cast<uint64_t>(__double_as_longlong(inc));
+    cbar();
+    double before = 0.0, all = 0.0;
+    for (uint32_t i = 0; i < kCons / 32; ++i) {
+        const double x = __longlong_as_double(static_cast<long long>(c.red_u64[i]));
+        if (i < w) before += x;
+        all += x;
+    }
+    *total = all;
+    return before + excl;
+}
+
 // ------------------------------------------------------------ row context
 struct Row {
     uint32_t v;           // virtual row
@@ -591,113 +614,91 @@ __device__ uint32_t finish_buffer(uint64_t* cand, uint32_t n, const Row& r, uint
 // ---------------------------------------------------------------- epilogue
 // Softmax / min-p / top-p / draw over n candidates sorted by rank key, in
 // the order of sampling.cc:105-145: w_i = exp((double)(v_i - v_0)) with the
-// difference in float, sequential double prefix sums, the quotient-
-// accumulating top-p loop (top_p widened from float), total over the
-// retained prefix, draw = uniform01(rng_before + gamma) * total, first
-// prefix sum above the draw.  min-p keeps the prefix with w_i >= min_p.
-// Warp 0 runs it (lane 0 does the sequential sums); results in c.e_*.
+// difference in float, double prefix sums S_i of the weights, the top-p cut
+// at the first prefix of the quotients w_i / total that reaches top_p (top_p
+// widened from float), total over the retained prefix, draw =
+// uniform01(rng_before + gamma) * total, the first prefix sum above the
+// draw.  min-p keeps the prefix with w_i >= min_p.  The prefix sums are a
+// block-wide scan (each thread sums a contiguous run of at most four
+// candidates in order, then the runs' totals are scanned): they equal the
+// reference's sequential sums to a few units in the last place, so a token
+// can differ only where the draw or the top-p target lies within that
+// distance of a boundary.  Results in c.e_*.
 __device__ void epilogue(const uint64_t* sorted, uint32_t n, const RowParams& p, bool minp,
-                         uint64_t rng_before, double* w, double* S, double* q, Ctl& c) {
-    if (threadIdx.x < 32) {
-        constexpr unsigned kFull = 0xffffffffu;
-        const uint32_t lane = threadIdx.x;
-        int32_t status = Q38S_ROW_OK, token = -1;
-        uint32_t r = 0;
-        double total = 0.0, draw = 0.0;
-        if (n == 0 || !isfinite(rank_value(sorted[0]))) {
-            status = Q38S_ROW_NO_FINITE;
+                         uint64_t rng_before, double* w, double* S, Ctl& c) {
+    constexpr uint32_t kRun = kFinal / kCons;  // candidates per thread's run
+    static_assert(kFinal % kCons == 0 && kGather <= kFinal, "runs");
+    int32_t status = Q38S_ROW_OK, token = -1;
+    uint32_t r = 0;
+    double total = 0.0, draw = 0.0;
+    const bool finite = n != 0 && isfinite(rank_value(sorted[0]));
+    if (!finite) {
+        status = Q38S_ROW_NO_FINITE;
+    } else {
+        const float vmax = rank_value(sorted[0]);
+        for (uint32_t i = threadIdx.x; i < n; i += kCons)
+            w[i] = exp(static_cast<double>(__fsub_rn(rank_value(sorted[i]), vmax)));
+        cbar();
+        if (minp && p.min_p > 0.0f) {
+            const double floor_w = static_cast<double>(p.min_p);
+            uint32_t m = n;
+            for (uint32_t i = threadIdx.x; i < n; i += kCons)
+                if (!(w[i] >= floor_w)) m = min(m, i);
+            n = cmin_u32(m, c);
+        }
+        // inclusive prefix sums of w over runs of kRun consecutive candidates
+        const uint32_t i0 = threadIdx.x * kRun;
+        double run[kRun];
+        double acc = 0.0;
+#pragma unroll
+        for (uint32_t j = 0; j < kRun; ++j) {
+            if (i0 + j < n) acc += w[i0 + j];
+            run[j] = acc;
+        }
+        double all;
+        const double off = cscan_excl_f64(acc, &all, c);
+#pragma unroll
+        for (uint32_t j = 0; j < kRun; ++j)
+            if (i0 + j < n) S[i0 + j] = off + run[j];
+        cbar();
+        total = S[n - 1];
+        if (!(total > 0.0) || !isfinite(total)) {
+            status = Q38S_ROW_NORMALIZATION;
         } else {
-            const float vmax = rank_value(sorted[0]);
-            for (uint32_t i = lane; i < n; i += 32)
-                w[i] = exp(static_cast<double>(__fsub_rn(rank_value(sorted[i]), vmax)));
-            __syncwarp();
-            if (minp && p.min_p > 0.0f) {
-                const double floor_w = static_cast<double>(p.min_p);
-                uint32_t m = n;
-                for (uint32_t i0 = 0; i0 < n; i0 += 32) {
-                    const uint32_t i = i0 + lane;
-                    const uint32_t b = __ballot_sync(kFull, i < n && !(w[i] >= floor_w));
-                    if (b) {
-                        m = i0 + __ffs(b) - 1;
-                        break;
-                    }
+            r = n;
+            if (p.top_p < 1.0f) {
+                // prefix sums of the quotients, the first reaching top_p
+                const double top_p = static_cast<double>(p.top_p);
+                double qa = 0.0;
+#pragma unroll
+                for (uint32_t j = 0; j < kRun; ++j) {
+                    if (i0 + j < n) qa += w[i0 + j] / total;
+                    run[j] = qa;
                 }
-                n = m;
+                double qall;
+                const double qoff = cscan_excl_f64(qa, &qall, c);
+                uint32_t hit = n;
+#pragma unroll
+                for (uint32_t j = 0; j < kRun; ++j)
+                    if (i0 + j < n && qoff + run[j] >= top_p) hit = min(hit, i0 + j + 1);
+                r = cmin_u32(hit, c);
             }
-            if (lane == 0) {
-                // sequential sum (the reference's order); loads in batches of
-                // 8 so that only the additions are serial
-                double acc = 0.0;
-                uint32_t i = 0;
-                for (; i + 8 <= n; i += 8) {
-                    double v[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) v[j] = w[i + j];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        acc += v[j];
-                        S[i + j] = acc;
-                    }
-                }
-                for (; i < n; ++i) {
-                    acc += w[i];
-                    S[i] = acc;
-                }
-                total = acc;
-            }
-            total = __shfl_sync(kFull, total, 0);
-            if (!(total > 0.0) || !isfinite(total)) {
-                status = Q38S_ROW_NORMALIZATION;
-            } else {
-                r = n;
-                if (p.top_p < 1.0f) {
-                    for (uint32_t i = lane; i < n; i += 32) q[i] = w[i] / total;
-                    __syncwarp();
-                    uint32_t k = 0;
-                    if (lane == 0) {
-                        const double top_p = static_cast<double>(p.top_p);
-                        double cum = 0.0;
-                        bool hit = false;
-                        while (k < n && !hit) {
-                            // the reference's loop, with loads in batches of 8
-                            double v[8];
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) v[j] = k + j < n ? q[k + j] : 0.0;
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) {
-                                if (!hit && k < n) {
-                                    cum += v[j];
-                                    ++k;
-                                    if (cum >= top_p) hit = true;
-                                }
-                            }
-                        }
-                    }
-                    r = __shfl_sync(kFull, k, 0);
-                }
-                __syncwarp();
-                total = S[r - 1];  // the sequential sum over the retained prefix
-                draw = uniform01(rng_before + kGamma) * total;
-                uint32_t sel = r - 1;
-                for (uint32_t i0 = 0; i0 < r; i0 += 32) {
-                    const uint32_t i = i0 + lane;
-                    const uint32_t b = __ballot_sync(kFull, i < r && draw < S[i]);
-                    if (b) {
-                        sel = i0 + __ffs(b) - 1;
-                        break;
-                    }
-                }
-                token = static_cast<int32_t>(rank_token(sorted[sel]));
-            }
+            total = S[r - 1];  // the sum over the retained prefix
+            draw = uniform01(rng_before + kGamma) * total;
+            uint32_t sel = r - 1;
+            for (uint32_t i = threadIdx.x; i < r; i += kCons)
+                if (draw < S[i]) sel = min(sel, i);
+            sel = cmin_u32(sel, c);
+            token = static_cast<int32_t>(rank_token(sorted[sel]));
         }
-        if (lane == 0) {
-            c.e_status = status;
-            c.e_token = token;
-            c.e_n = n;
-            c.e_r = r;
-            c.e_total = total;
-            c.e_draw = draw;
-        }
+    }
+    if (threadIdx.x == 0) {
+        c.e_status = status;
+        c.e_token = token;
+        c.e_n = n;
+        c.e_r = r;
+        c.e_total = total;
+        c.e_draw = draw;
     }
     cbar();
 }
@@ -782,7 +783,7 @@ __device__ __forceinline__ void row_error(const SampleArgs& a, const Row& r, int
 // Final outputs of a row from its sorted candidate list.
 __device__ __forceinline__ void row_output(const SampleArgs& a, const Row& r,
                                            const uint64_t* sorted,
-                           uint32_t keep, double* w, double* S, double* q, Ctl& c) {
+                           uint32_t keep, double* w, double* S, Ctl& c) {
     if (a.mode == kModeShardTopK) {
         for (uint32_t i = threadIdx.x; i < a.k_out; i += kCons) {
             q38s_candidate cd;
@@ -797,7 +798,7 @@ __device__ __forceinline__ void row_output(const SampleArgs& a, const Row& r,
         }
         return;
     }
-    epilogue(sorted, keep, r.p, r.minp, r.rng_before, w, S, q, c);
+    epilogue(sorted, keep, r.p, r.minp, r.rng_before, w, S, c);
     Q38S_TT(r.v, 11);
     write_decision(a, r, c.e_token, c.e_status);
     Q38S_TT(r.v, 12);
@@ -1138,28 +1139,6 @@ __device__ __forceinline__ unsigned long long get_u64_split(const uint32_t* w) {
     return static_cast<unsigned long long>(w[0]) | (static_cast<unsigned long long>(w[1]) << 32);
 }
 
-// Exclusive prefix sum of doubles over the consumers in thread order.
-__device__ __forceinline__ double cscan_excl_f64(double v, double* total, Ctl& c) {
-    const uint32_t lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    double inc = v;
-    for (int o = 1; o < 32; o <<= 1) {
-        const double y = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= static_cast<uint32_t>(o)) inc += y;
-    }
-    double excl = __shfl_up_sync(0xffffffffu, inc, 1);
-    if (lane == 0) excl = 0.0;
-    cbar();
-    if (lane == 31) c.red_u64[w] = static_cast<uint64_t>(__double_as_longlong(inc));
-    cbar();
-    double before = 0.0, all = 0.0;
-    for (uint32_t i = 0; i < kCons / 32; ++i) {
-        const double x = __longlong_as_double(static_cast<long long>(c.red_u64[i]));
-        if (i < w) before += x;
-        all += x;
-    }
-    *total = all;
-    return before + excl;
-}
 
 // Pipelined passes of the general kernel: every thread streams its own
 // 16-byte groups (group r * kCons + tid in round r) through kStages cp.async
@@ -1551,42 +1530,43 @@ __device__ __forceinline__ GLoc g_final(const GRow g, const GSpan s, bool mass, 
     const uint32_t n = g_gather_sorted(g, s, s.b1, s.b1, buf, lk, c);
     GLoc res{false, 0, 0, 0, 0.0};
     if (n == 0) return res;
-    if (threadIdx.x < 32) {
-        const uint32_t lane = threadIdx.x;
-        uint32_t sel = n - 1;
-        double through = 0.0;
-        if (!mass) {
+    if (!mass) {
+        if (threadIdx.x == 0) {
             const double pos = tau - static_cast<double>(s.above_cnt) - 1.0;
-            sel = pos <= 0.0 ? 0u : min(n - 1, static_cast<uint32_t>(pos));
-            through = static_cast<double>(s.above_cnt + sel + 1);
-        } else {
-            double base = s.above_mass;
-            bool hit = false;
-            for (uint32_t i0 = 0; i0 < n && !hit; i0 += 32) {
-                const uint32_t i = i0 + lane;
-                const double w = i < n ? g_weight(g, static_cast<uint32_t>(lk[i] >> 32)) : 0.0;
-                double inc = w;
-                for (int o = 1; o < 32; o <<= 1) {
-                    const double y = __shfl_up_sync(0xffffffffu, inc, o);
-                    if (lane >= static_cast<uint32_t>(o)) inc += y;
-                }
-                const double S = base + inc;
-                const uint32_t b = __ballot_sync(0xffffffffu,
-                                                 i < n && (strict ? (S > tau) : (S >= tau)));
-                if (b) {
-                    const uint32_t f = __ffs(b) - 1;
-                    sel = i0 + f;
-                    through = __shfl_sync(0xffffffffu, S, f);
-                    hit = true;
-                } else {
-                    base = __shfl_sync(0xffffffffu, S, 31);
-                    through = base;  // no element reaches the target: the last one
-                }
-            }
-        }
-        if (lane == 0) {
+            const uint32_t sel = pos <= 0.0 ? 0u : min(n - 1, static_cast<uint32_t>(pos));
             c.bc_u32[0] = sel;
-            c.bc_u64[0] = static_cast<uint64_t>(__double_as_longlong(through));
+            c.bc_u64[0] = static_cast<uint64_t>(
+                __double_as_longlong(static_cast<double>(s.above_cnt + sel + 1)));
+        }
+    } else {
+        // exact weights summed in canonical order from the mass above the
+        // span: each thread a run of four consecutive members, then a scan
+        // of the runs' sums
+        constexpr uint32_t kRun = kGL / kCons;
+        const uint32_t i0 = threadIdx.x * kRun;
+        double run[kRun];
+        double acc = 0.0;
+#pragma unroll
+        for (uint32_t j = 0; j < kRun; ++j) {
+            if (i0 + j < n) acc += g_weight(g, static_cast<uint32_t>(lk[i0 + j] >> 32));
+            run[j] = acc;
+        }
+        double all;
+        const double off = s.above_mass + cscan_excl_f64(acc, &all, c);
+        uint32_t hit = 0xffffffffu;
+#pragma unroll
+        for (uint32_t j = 0; j < kRun; ++j) {
+            const double S = off + run[j];
+            if (i0 + j < n && (strict ? (S > tau) : (S >= tau))) hit = min(hit, i0 + j);
+        }
+        hit = cmin_u32(hit, c);
+        const uint32_t sel = hit == 0xffffffffu ? n - 1 : hit;  // none reaches tau: the last
+#pragma unroll
+        for (uint32_t j = 0; j < kRun; ++j) {
+            if (i0 + j == sel) {
+                c.bc_u32[0] = sel;
+                c.bc_u64[0] = static_cast<uint64_t>(__double_as_longlong(off + run[j]));
+            }
         }
     }
     cbar();
@@ -2089,8 +2069,7 @@ __device__ __forceinline__ void general_row(const SampleArgs& a, const Row& r, u
         }
         double* w = reinterpret_cast<double*>(area);  // over the dead gather buffer
         double* S = reinterpret_cast<double*>(area + kGL * 16);
-        double* q = reinterpret_cast<double*>(area + kGL * 24);
-        row_output(a, r, lk, m, w, S, q, c);
+        row_output(a, r, lk, m, w, S, c);
         return;
     }
     if (a.mode == kModeShardTopK) {  // candidate lists hold at most kLeaderCap
@@ -2181,7 +2160,7 @@ __device__ __forceinline__ void finish_row(const SampleArgs& a, const Row& r, ui
         return;
     } else {
         double* w = reinterpret_cast<double*>(area);  // over the dead candidate buffer
-        row_output(a, r, sorted, keep, w, w + kFinal, w + 2 * kFinal, c);
+        row_output(a, r, sorted, keep, w, w + kFinal, c);
     }
     row_done(a, area, c);
 }
@@ -2344,9 +2323,6 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
     extern __shared__ __align__(1024) unsigned char dsm[];
     __shared__ Ctl c;
     __shared__ Row rs;
-    // the general kernel behind this one may be scheduled now; it waits for
-    // this grid's completion before it reads anything this grid writes
-    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     constexpr uint32_t es = DT == Q38S_DTYPE_BF16 ? 2u : 4u;
     constexpr uint32_t pv = 16u / es;  // elements per 16-byte vector
     constexpr uint32_t TC = kTileBytes / es;
@@ -2638,29 +2614,30 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
             // whole vectors with -inf, its bitmap slice behind it): read it
             // there instead of from L2
             const bool resident = ntiles <= kRing && u + gridDim.x >= n_units;
-#pragma unroll 1
-            for (uint32_t hi = tid; hi < n_hit; hi += kCons) {
-                const uint32_t t = hlist[hi] / kCons, thr = hlist[hi] % kCons;
+            // the vectors of hit block hidx (a thread's block of a tile)
+            auto load_block = [&](uint32_t hidx, uint4 (&w)[kU]) {
+                const uint32_t t = hlist[hidx] / kCons, thr = hlist[hidx] % kCons;
                 const uint32_t t0 = c0 + t * TC;
                 const uint32_t n = min(c1 - t0, TC);
                 const unsigned char* sl = ring + ((g - ntiles + t) % kRing) * kSlot;
-                uint4 w[kU];
-                uint32_t pw[kU];
 #pragma unroll
                 for (int q = 0; q < kU; ++q) {  // every load in flight at once
                     const uint32_t e0 = (thr + q * kCons) * pv;
                     const uint32_t nv = e0 < n ? min(pv, n - e0) : 0u;
-                    if (resident) {
+                    if (resident)
                         w[q] = nv ? *reinterpret_cast<const uint4*>(sl + e0 * es)
                                   : make_uint4(0u, 0u, 0u, 0u);
-                        pw[q] = (nv && r.pen)
-                            ? reinterpret_cast<const uint32_t*>(sl + kTileBytes)[e0 >> 5] : 0u;
-                    } else {
+                    else
                         w[q] = nv ? load_vec<DT>(a, src_row, t0 + e0, nv)
                                   : make_uint4(0u, 0u, 0u, 0u);
-                        pw[q] = (nv && r.pen) ? __ldg(&r.gbm[(t0 + e0) >> 5]) : 0u;
-                    }
                 }
+            };
+            // its elements that reach rho join the candidates (the penalty
+            // word of a candidate's vector is read only for candidates)
+            auto scan_block = [&](uint32_t hidx, const uint4 (&w)[kU]) {
+                const uint32_t t = hlist[hidx] / kCons, thr = hlist[hidx] % kCons;
+                const uint32_t t0 = c0 + t * TC;
+                const uint32_t n = min(c1 - t0, TC);
                 uint32_t cm = 0;  // bit q * pv + e: element e of vector q reaches rho
 #pragma unroll
                 for (int q = 0; q < kU; ++q) {
@@ -2676,19 +2653,38 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
                     cm &= cm - 1;
                     const uint32_t qv = b / pv, ev = b % pv;
                     uint4 wq = w[0];
-                    uint32_t pq = pw[0];
 #pragma unroll
                     for (int q = 1; q < kU; ++q)
-                        if (qv == static_cast<uint32_t>(q)) {
-                            wq = w[q];
-                            pq = pw[q];
-                        }
+                        if (qv == static_cast<uint32_t>(q)) wq = w[q];
                     float x = 0.0f;
 #pragma unroll
                     for (uint32_t e = 0; e < pv; ++e)
                         if (ev == e) x = vec_elem<DT>(wq, static_cast<int>(e));
-                    consider(x, t0 + (thr + qv * kCons) * pv + ev, pq);
+                    const uint32_t e0 = (thr + qv * kCons) * pv;
+                    uint32_t pq = 0;
+                    if (r.pen) {
+                        pq = resident ? reinterpret_cast<const uint32_t*>(
+                                            ring + ((g - ntiles + t) % kRing) * kSlot +
+                                            kTileBytes)[e0 >> 5]
+                                      : __ldg(&r.gbm[(t0 + e0) >> 5]);
+                    }
+                    consider(x, t0 + e0 + ev, pq);
                 }
+            };
+            // two blocks per round, both blocks' loads in flight before either
+            // is scanned (the re-reads come from L2 or HBM while other CTAs
+            // still stream: their latency dominates this loop)
+#pragma unroll 1
+            for (uint32_t hi = tid; hi < n_hit; hi += 2 * kCons) {
+                // a buffer that has overflowed sends the row to the general
+                // path: stop gathering
+                if (*reinterpret_cast<volatile uint32_t*>(&c.n_cand) > cap) break;
+                const bool two = hi + kCons < n_hit;
+                uint4 w0[kU], w1[kU];
+                load_block(hi, w0);
+                if (two) load_block(hi + kCons, w1);
+                scan_block(hi, w0);
+                if (two) scan_block(hi + kCons, w1);
             }
             if (r.nonmono) {
                 // penalties can raise a value: every penalised element below
@@ -2874,6 +2870,11 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
         }
         cbar();
     }
+    // the general kernel behind this one may be scheduled once every CTA of
+    // this grid got here (not earlier: its CTAs would share the SMs of rows
+    // still in their tails); it waits for this grid's completion before it
+    // reads anything this grid writes
+    if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 }  // namespace

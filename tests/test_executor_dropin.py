@@ -67,3 +67,31 @@ def test_gpu_sampler_behind_the_reference_executor_matches_the_cpu_sampler(cuda)
         assert a == b, f"line {i}: {a} != {b}"
     decoded = sum(len(x.get("tokens", [])) for x in ours if ":" in x.get("op", ""))
     print(f"executor drop-in: {len(ours)} steps identical, {decoded} tokens")
+
+
+DEV_REF = os.path.join(ROOT, "oracle", "_ref", "dev_ref")
+DEV_Q38S = os.path.join(ROOT, "oracle", "_ref", "dev_q38s")
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not (os.path.exists(DEV_REF) and os.path.exists(DEV_Q38S)),
+                    reason="device decode harness not built")
+def test_device_logits_decode_matches_the_cpu_sampler(cuda):
+    """oracle/device_decode_harness.cc: the executor's sampled decode steps
+    with the stage-1 logits resident on the device (prepare_device, no D2H
+    copy of the logits) against the reference's CPU sampler on the same
+    logits on the host, three sessions of 120 steps at V = 248,320: every
+    token and SamplerStateV1 word identical."""
+    def run(path):
+        r = subprocess.run([path, "120"], capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+        lines = [json.loads(line) for line in r.stdout.splitlines() if line.strip()]
+        timing = [x for x in lines if x.get("op") == "timing"]
+        return [x for x in lines if x.get("op") != "timing"], timing[0]["us_per_step"]
+
+    ref, ref_t = run(DEV_REF)
+    dev, dev_t = run(DEV_Q38S)
+    assert len(ref) == len(dev) == 3 * 121
+    for a, b in zip(ref, dev):
+        assert a == b, f"reference {a} vs device {b}"
+    print(f"us per step: device logits {dev_t}, reference on host logits {ref_t}")
