@@ -2323,6 +2323,10 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
     extern __shared__ __align__(1024) unsigned char dsm[];
     __shared__ Ctl c;
     __shared__ Row rs;
+    // the general kernel behind this one may be scheduled now, onto SMs this
+    // grid leaves free; it waits for this grid's completion before it reads
+    // anything this grid writes
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     constexpr uint32_t es = DT == Q38S_DTYPE_BF16 ? 2u : 4u;
     constexpr uint32_t pv = 16u / es;  // elements per 16-byte vector
     constexpr uint32_t TC = kTileBytes / es;
@@ -2870,11 +2874,6 @@ __global__ void __launch_bounds__(kBlock, 2) stream_kernel(const SampleArgs a) {
         }
         cbar();
     }
-    // the general kernel behind this one may be scheduled once every CTA of
-    // this grid got here (not earlier: its CTAs would share the SMs of rows
-    // still in their tails); it waits for this grid's completion before it
-    // reads anything this grid writes
-    if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 }  // namespace
@@ -2918,7 +2917,8 @@ void set_stream_fault(uint32_t withhold, long long wait_cycles) {
 // The general kernel behind every stream kernel, as its programmatic
 // dependent (the launch overlaps the stream kernel).
 template <int DT>
-static cudaError_t launch_general(const SampleArgs& a, void* stream, int sms) {
+static cudaError_t launch_general(const SampleArgs& a, void* stream, int sms,
+                                  uint32_t stream_grid) {
     static bool configured[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -2931,10 +2931,15 @@ static cudaError_t launch_general(const SampleArgs& a, void* stream, int sms) {
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    // one CTA per SM (its shared memory admits no second): every CTA of a
-    // team is resident once the stream kernel has left the SMs
+    // at most one CTA per SM (its registers admit no second, nor a stream
+    // CTA beside it): every CTA of a team is resident once the stream kernel
+    // has left the SMs.  A stream grid smaller than the SM count leaves SMs
+    // free: the general grid takes exactly those, so that all of its CTAs are
+    // resident (waiting) before the stream kernel ends
+    const uint32_t n = static_cast<uint32_t>(sms);
+    const uint32_t grid = stream_grid < n ? n - stream_grid : n;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<uint32_t>(sms));
+    cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kCons);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
@@ -2982,7 +2987,8 @@ static int launch_stream_t(const SampleArgs& a_in, void* stream) {
     if (a.segs == 1) {
         kern<<<grid, kBlock, smem, static_cast<cudaStream_t>(stream)>>>(a);
         e = cudaGetLastError();
-        return (e != cudaSuccess || a.host_general) ? e : launch_general<DT>(a, stream, sms[dev]);
+        return (e != cudaSuccess || a.host_general) ? e
+                                                     : launch_general<DT>(a, stream, sms[dev], grid);
     }
     // one cluster of segs CTAs per row: CTA rank = segment
     cudaLaunchConfig_t cfg = {};
@@ -2998,7 +3004,8 @@ static int launch_stream_t(const SampleArgs& a_in, void* stream) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, kern, a);
-    return (e != cudaSuccess || a.host_general) ? e : launch_general<DT>(a, stream, sms[dev]);
+    return (e != cudaSuccess || a.host_general) ? e
+                                                 : launch_general<DT>(a, stream, sms[dev], grid);
 }
 
 int launch_general_only(const SampleArgs& a, void* stream) {
@@ -3008,8 +3015,8 @@ int launch_general_only(const SampleArgs& a, void* stream) {
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
-    return a.dtype == Q38S_DTYPE_BF16 ? launch_general<Q38S_DTYPE_BF16>(a, stream, sms)
-                                      : launch_general<Q38S_DTYPE_F32>(a, stream, sms);
+    return a.dtype == Q38S_DTYPE_BF16 ? launch_general<Q38S_DTYPE_BF16>(a, stream, sms, 0)
+                                      : launch_general<Q38S_DTYPE_F32>(a, stream, sms, 0);
 }
 
 int launch_stream(const SampleArgs& a, void* stream) {

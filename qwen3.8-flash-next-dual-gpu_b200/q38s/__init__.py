@@ -218,9 +218,13 @@ class Sampler:
         self._commit_tokens = L.q38s_sampler_commit_tokens
 
     def close(self):
-        if getattr(self, "_h", None):
-            lib().q38s_sampler_destroy(self._h)
+        h = getattr(self, "_h", None)
+        if h:
             self._h = None
+            try:
+                lib().q38s_sampler_destroy(h)
+            except TypeError:  # interpreter shutdown: the module is gone already
+                pass
 
     __del__ = close
 
@@ -304,9 +308,13 @@ class Batch:
         self.configs = list(configs)
 
     def close(self):
-        if getattr(self, "_h", None):
-            lib().q38s_batch_destroy(self._h)
+        h = getattr(self, "_h", None)
+        if h:
             self._h = None
+            try:
+                lib().q38s_batch_destroy(h)
+            except TypeError:  # interpreter shutdown: the module is gone already
+                pass
 
     __del__ = close
 
