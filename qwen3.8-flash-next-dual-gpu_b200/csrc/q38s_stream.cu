@@ -1521,6 +1521,41 @@ __device__ __forceinline__ uint32_t g_gather_sorted(const GRow g, const GSpan s,
     return n;
 }
 
+// The first of n members lk[0..n) (sorted, canonical order) at which the
+// mass, summed from `above` with exact weights in canonical order, reaches
+// tau (> tau when strict); the last member when none does.  Each thread sums
+// a run of four consecutive members, then the runs' sums are scanned.  The
+// member's index goes to c.bc_u32[0] and the mass through it to c.bc_u64[0].
+__device__ __forceinline__ void g_scan_mass(const GRow g, const uint64_t* lk, uint32_t n,
+                                            double above, double tau, bool strict, Ctl& c) {
+    constexpr uint32_t kRun = kGL / kCons;
+    const uint32_t i0 = threadIdx.x * kRun;
+    double run[kRun];
+    double acc = 0.0;
+#pragma unroll
+    for (uint32_t j = 0; j < kRun; ++j) {
+        if (i0 + j < n) acc += g_weight(g, static_cast<uint32_t>(lk[i0 + j] >> 32));
+        run[j] = acc;
+    }
+    double all;
+    const double off = above + cscan_excl_f64(acc, &all, c);
+    uint32_t hit = 0xffffffffu;
+#pragma unroll
+    for (uint32_t j = 0; j < kRun; ++j) {
+        const double S = off + run[j];
+        if (i0 + j < n && (strict ? (S > tau) : (S >= tau))) hit = min(hit, i0 + j);
+    }
+    hit = cmin_u32(hit, c);
+    const uint32_t sel = hit == 0xffffffffu ? n - 1 : hit;
+#pragma unroll
+    for (uint32_t j = 0; j < kRun; ++j) {
+        if (i0 + j == sel) {
+            c.bc_u32[0] = sel;
+            c.bc_u64[0] = static_cast<uint64_t>(__double_as_longlong(off + run[j]));
+        }
+    }
+}
+
 // The located element inside a span of at most kGL members: exact weights
 // summed in canonical order from the mass above the span.
 __device__ __forceinline__ GLoc g_final(const GRow g, const GSpan s, bool mass, double tau, bool strict,
@@ -1539,35 +1574,7 @@ __device__ __forceinline__ GLoc g_final(const GRow g, const GSpan s, bool mass, 
                 __double_as_longlong(static_cast<double>(s.above_cnt + sel + 1)));
         }
     } else {
-        // exact weights summed in canonical order from the mass above the
-        // span: each thread a run of four consecutive members, then a scan
-        // of the runs' sums
-        constexpr uint32_t kRun = kGL / kCons;
-        const uint32_t i0 = threadIdx.x * kRun;
-        double run[kRun];
-        double acc = 0.0;
-#pragma unroll
-        for (uint32_t j = 0; j < kRun; ++j) {
-            if (i0 + j < n) acc += g_weight(g, static_cast<uint32_t>(lk[i0 + j] >> 32));
-            run[j] = acc;
-        }
-        double all;
-        const double off = s.above_mass + cscan_excl_f64(acc, &all, c);
-        uint32_t hit = 0xffffffffu;
-#pragma unroll
-        for (uint32_t j = 0; j < kRun; ++j) {
-            const double S = off + run[j];
-            if (i0 + j < n && (strict ? (S > tau) : (S >= tau))) hit = min(hit, i0 + j);
-        }
-        hit = cmin_u32(hit, c);
-        const uint32_t sel = hit == 0xffffffffu ? n - 1 : hit;  // none reaches tau: the last
-#pragma unroll
-        for (uint32_t j = 0; j < kRun; ++j) {
-            if (i0 + j == sel) {
-                c.bc_u32[0] = sel;
-                c.bc_u64[0] = static_cast<uint64_t>(__double_as_longlong(off + run[j]));
-            }
-        }
+        g_scan_mass(g, lk, n, s.above_mass, tau, strict, c);
     }
     cbar();
     const uint32_t sel = c.bc_u32[0];
@@ -1636,12 +1643,14 @@ __device__ __forceinline__ GLoc g_tie(const GRow g, const GSpan s, bool mass, do
     return res;
 }
 
-// First K0 element at which the running count (mass false: tau an integer
-// count) or mass reaches tau (>= tau, or > tau when strict).
-__device__ __forceinline__ GLoc g_locate(const GRow g, const uint32_t* pc, const double* pm, bool mass,
-                         double tau, bool strict, unsigned char* area, Ctl& c) {
+// The level-1 bin in which the running count (mass false: tau an integer
+// count) or mass first reaches tau (>= tau, or > tau when strict): the first
+// non-empty bin whose prefix through it reaches tau, else (rounding: the
+// target lies past the last bin) the last non-empty bin; 0xffffffff when K0
+// is empty.
+__device__ __forceinline__ uint32_t g_bin_of(const uint32_t* pc, const double* pm, bool mass,
+                                             double tau, bool strict, Ctl& c) {
     constexpr uint32_t kPer = kGB / kCons;
-    // the bin: first b whose running total through it reaches tau
     uint32_t first = 0xffffffffu;
 #pragma unroll
     for (uint32_t j = 0; j < kPer; ++j) {
@@ -1651,16 +1660,25 @@ __device__ __forceinline__ GLoc g_locate(const GRow g, const uint32_t* pc, const
         if (hit && first == 0xffffffffu && pc[b + 1] > pc[b]) first = b;
     }
     first = cmin_u32(first, c);
-    if (first == 0xffffffffu) {  // rounding: the target lies past the last bin
+    if (first == 0xffffffffu) {
         uint32_t last = 0;
         for (uint32_t j = 0; j < kPer; ++j) {
             const uint32_t b = threadIdx.x * kPer + j;
             if (pc[b + 1] > pc[b]) last = b + 1;
         }
         last = cmax_u32(last, c);
-        if (last == 0) return GLoc{false, 0, 0, 0, 0.0};
-        first = last - 1;
+        first = last == 0 ? 0xffffffffu : last - 1;
     }
+    return first;
+}
+
+// First K0 element at which the running count (mass false: tau an integer
+// count) or mass reaches tau (>= tau, or > tau when strict).
+__device__ __forceinline__ GLoc g_locate(const GRow g, const uint32_t* pc, const double* pm, bool mass,
+                         double tau, bool strict, unsigned char* area, Ctl& c) {
+    constexpr uint32_t kPer = kGB / kCons;
+    const uint32_t first = g_bin_of(pc, pm, mass, tau, strict, c);
+    if (first == 0xffffffffu) return GLoc{false, 0, 0, 0, 0.0};
     GSpan s;
     s.b1 = first;
     s.lo = 0;
@@ -2931,15 +2949,13 @@ static cudaError_t launch_general(const SampleArgs& a, void* stream, int sms,
         if (e != cudaSuccess) return e;
         configured[dev] = true;
     }
-    // at most one CTA per SM (its registers admit no second, nor a stream
-    // CTA beside it): every CTA of a team is resident once the stream kernel
-    // has left the SMs.  A stream grid smaller than the SM count leaves SMs
-    // free: the general grid takes exactly those, so that all of its CTAs are
-    // resident (waiting) before the stream kernel ends
-    const uint32_t n = static_cast<uint32_t>(sms);
-    const uint32_t grid = stream_grid < n ? n - stream_grid : n;
+    // one CTA per SM (its registers admit no second, nor a stream CTA beside
+    // it): every CTA of a team is resident once the stream kernel has left
+    // the SMs.  (A grid of only the SMs a small stream grid leaves free made
+    // batch-1 no faster and split 16 deferred rows into teams of one.)
+    (void)stream_grid;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
+    cfg.gridDim = dim3(static_cast<uint32_t>(sms));
     cfg.blockDim = dim3(kCons);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
