@@ -29,7 +29,6 @@ from __future__ import annotations
 
 import importlib.util
 import json
-import os
 import shutil
 import sys
 from pathlib import Path
@@ -43,11 +42,15 @@ import oracle as O  # noqa: E402
 from q38s import synth  # noqa: E402
 
 OUT = Path(__file__).resolve().parent / "logit_captures"
-REF = Path(os.environ.get("Q38S_REFERENCE_ROOT", "/root/reference"))
+sys.path.insert(0, str(ROOT))
+from __graft_entry__ import reference_root  # noqa: E402  (the reference checkout, if any)
 
 
 def ref_tool():
-    tools = REF / "tools"
+    root = reference_root()
+    if root is None:
+        raise SystemExit("the reference sources are needed: set Q38S_REFERENCE_ROOT")
+    tools = Path(root) / "tools"
     sys.path.insert(0, str(tools))  # the tool imports its RPC client beside it
     spec = importlib.util.spec_from_file_location("q38_logit_parity",
                                                   tools / "q38_logit_parity.py")
