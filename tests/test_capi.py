@@ -73,6 +73,18 @@ def test_host_validation_without_gpu():
     assert L.q38s_topk_router_bf16(None, None, None, 1, 512, 10, 1, None, 0) == \
         q38s.INVALID_ARGUMENT
     assert L.q38s_last_error().decode() == "invalid top-k router buffers"
+    fake = C.c_void_p(16)  # never dereferenced: every check below fails first
+    for args, msg in (((1, 512, 33, 1), "invalid top-k router buffers"),
+                      ((1, 8, 9, 1), "invalid top-k router buffers"),
+                      ((0, 512, 10, 1), "invalid top-k router buffers"),
+                      ((1, 4000, 10, 1), "router experts above 3,072 per token")):
+        tokens, experts, top_k, norm = args
+        assert L.q38s_topk_router_bf16(fake, fake, fake, tokens, experts, top_k, norm, None,
+                                       0) == q38s.INVALID_ARGUMENT
+        assert L.q38s_last_error().decode() == msg
+    assert L.q38s_topk_router_bf16(fake, fake, fake, 1, 512, 10, 1, None, -1) == \
+        q38s.INVALID_ARGUMENT
+    assert L.q38s_last_error().decode() == "invalid CUDA kernel launch context"
     wide = q38s.config_v1(top_k=20)
     assert L.q38s_sampler_create(0, (1 << 20) + 1, C.byref(wide), C.byref(h)) == \
         q38s.INVALID_ARGUMENT
