@@ -1219,7 +1219,11 @@ __device__ __forceinline__ uint32_t* team_acc(const GTeam& t) {
     return t.slots + (t.phase % 3u) * kSlotWords;
 }
 // Every member's partial results of the phase are in: the barrier, then the
-// zeroing of the slot after next.  Returns the slot that holds the totals,
+// zeroing of the slot after next.  The CTA barrier orders every thread's
+// partial results before thread 0's acquire-release arrival (release is
+// cumulative), and the acquire of the new generation plus the CTA barrier
+// after it order the other members' results before this CTA's L2 reads, so
+// no separate fence is needed.  Returns the slot that holds the totals,
 // or nullptr when this CTA has left the team (its wait ran out now or
 // before); a CTA that left neither adds nor waits any more, so the others'
 // next wait runs out as well and the row ends with a timeout status.
@@ -1228,7 +1232,6 @@ __device__ __forceinline__ const uint32_t* team_sync(GTeam& t, Ctl& c) {
     cbar();  // the CTA's partial results are issued
     if (threadIdx.x == 0) {
         if (!t.failed) {
-            __threadfence();
             const uint32_t gen = ld_acquire_gpu(t.sync + 1);
             if (atom_add_acq_rel_gpu(t.sync, 1u) + 1u == t.size) {
                 t.sync[0] = 0;  // before the release: the next barrier counts from 0
@@ -1242,7 +1245,6 @@ __device__ __forceinline__ const uint32_t* team_sync(GTeam& t, Ctl& c) {
                     }
                 }
             }
-            __threadfence();
         }
         ++t.phase;
     }
