@@ -146,3 +146,11 @@ def test_manifest_rejections(tmp_path):
     put(dict(meta, sha256=hashlib.sha256(bytes(bad)).hexdigest()))
     with pytest.raises(ValueError, match="FNV-1a does not match"):
         cap.read_capture(path)
+
+
+def test_cli_check_without_captures(tmp_path, capsys):
+    """`python -m q38s.capture check DIR` on a directory without captures
+    reports none and exits 1 (no GPU is touched)."""
+    (tmp_path / "notes.json").write_text('{"schema": "other"}')
+    assert cap.main(["check", str(tmp_path)]) == 1
+    assert json.loads(capsys.readouterr().out) == {"captures": 0}
